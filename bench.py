@@ -1,0 +1,429 @@
+"""Thunder scan benchmark (GB/s and fraction of the measured HBM roofline).
+
+Workload: the raw scan microbenchmark -- A, B of shape [B,T,H,D] =
+[32, 4096, 16, 64] (the reference layout of [batch=32, heads=16, T=4096, d=64]),
+A = sigmoid(2 N(0,1) + 2), B ~ N(0,1), E_0 = 0, fp16, compass 16.
+One step = one forward scan of the whole tensor (kernel a).  Inputs (537 MB)
+and output (268 MB) exceed the 126 MB L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun, one rank per GPU): batch x head sharding, every rank scans its
+own [32,4096,16,64] tensor (independent channels, no collective): weak scaling,
+value = all ranks' bytes / max-over-ranks device time.
+
+Reference arm (--impl reference): the reference's CPU path for this workload
+(its chunked Thunder scan restated in oracle/oracle.py, torch on all host
+cores, fp32 -- the reference's CPU dtype for precision fp16) on a bounded
+batch slice per step; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "entangled-state-attention_v2_b200"))
+sys.path.insert(0, str(ROOT))
+
+SHAPE = (32, 4096, 16, 64)
+METRIC = "thunder_scan_fwd_GBps"
+UNIT = "GB/s"
+WORKLOAD = "thunder_scan fwd [B,T,H,D]=[32,4096,16,64] fp16 compass=16"
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic_summary():
+    p = ROOT / "profiles" / "roofline_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampled every 100 ms while the timed region runs."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                sms.append(float(parts[2]))
+                mx = float(parts[3])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[6:10]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def cpu_baseline(target_s: float = 12.0, max_rows: int = 32) -> dict:
+    """The reference's CPU Thunder scan (restated in the oracle), fp32, all
+    host threads, on a batch slice of the workload; GB/s of algorithmic bytes."""
+    import torch
+
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    _, T, H, D = SHAPE
+    rows = 1
+    A = torch.sigmoid(torch.randn(rows, T, H, D, generator=g) * 2 + 2)
+    B = torch.randn(rows, T, H, D, generator=g)
+    oracle.thunder_scan_port(A, B, 16)  # warm-up
+    t0 = time.perf_counter()
+    oracle.thunder_scan_port(A, B, 16)
+    one = time.perf_counter() - t0
+    rows = int(max(1, min(max_rows, target_s / max(one, 1e-3) / 3)))
+    A = torch.sigmoid(torch.randn(rows, T, H, D, generator=g) * 2 + 2)
+    B = torch.randn(rows, T, H, D, generator=g)
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        oracle.thunder_scan_port(A, B, 16)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    nbytes = 3 * A.numel() * 4
+    return {"value": nbytes / t / 1e9, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"thunder_scan restatement (oracle.thunder_scan_port, torch eager CPU, fp32, "
+                      f"compass 16) on a [{rows},{T},{H},{D}] batch slice, median of 3, "
+                      f"{t:.2f} s each"}
+
+
+def run_reference(args) -> None:
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return
+    import torch
+
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    _, T, H, D = SHAPE
+    g = torch.Generator().manual_seed(0)
+    # size each step's slice so that warmup + steps stay within ~2 minutes
+    A1 = torch.sigmoid(torch.randn(1, T, H, D, generator=g) * 2 + 2)
+    B1 = torch.randn(1, T, H, D, generator=g)
+    oracle.thunder_scan_port(A1, B1, 16)
+    t0 = time.perf_counter()
+    oracle.thunder_scan_port(A1, B1, 16)
+    one = max(time.perf_counter() - t0, 1e-4)
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    Tn = T
+    if one > budget:
+        Tn = max(64, int(T * budget / one) // 64 * 64)
+    A = A1[:, :Tn].contiguous()
+    B = B1[:, :Tn].contiguous()
+    for _ in range(args.warmup):
+        oracle.thunder_scan_port(A, B, 16)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.thunder_scan_port(A, B, 16)
+    el = time.perf_counter() - t0
+    nbytes = 3 * A.numel() * 4
+    val = nbytes * args.steps / el / 1e9
+    sample = (f"thunder_scan restatement (torch eager CPU, fp32, compass 16) on a [1,{Tn},{H},{D}] "
+              f"slice of the [32,4096,16,64] workload per step")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)", "config": {"workload": WORKLOAD, "cpu_sample": sample},
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from esa import _lib, ops
+    from esa.backends.thunder import thunder_scan
+
+    ws, rank, local = _dist()
+    if args.gpus != ws and ws > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={ws}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(dev)
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    A = torch.sigmoid(torch.randn(SHAPE, device=dev, generator=gen) * 2 + 2).half()
+    B = torch.randn(SHAPE, device=dev, generator=gen).half()
+    E = torch.empty_like(A)
+    nb, T, H, D = SHAPE
+    hd = H * D
+    N = A.numel()
+    compass = 16
+    wsb = L.esa_scan_workspace_bytes(nb, T, hd, _lib.DTYPE_F16, compass)
+    wsp = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    sp = stream.cuda_stream
+
+    def step():
+        rc = L.esa_scan_fwd(A.data_ptr(), B.data_ptr(), E.data_ptr(), nb, T, hd, _lib.DTYPE_F16,
+                            compass, None, None, wsp.data_ptr(), wsb, sp)
+        if rc:
+            raise RuntimeError(_lib.last_error())
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    ev[0].record(stream)
+    for i in range(args.steps):
+        step()
+        ev[i + 1].record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    clk = clocks.stop()
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    total_ms = ev[0].elapsed_time(ev[-1])
+    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    alg_bytes = 3 * N * 2
+    value = ws * alg_bytes * args.steps / (total_ms * 1e-3) / 1e9
+    mean_launch_ms = statistics.mean(per)
+    peak, peak_kind = _peaks()
+    achieved = alg_bytes / (mean_launch_ms * 1e-3) / 1e9
+    ops.check_device_status(dev)
+
+    # correctness spot check of the timed output (a few channels vs fp32 torch)
+    ref_ch = A[0, :, 0, :8].float(), B[0, :, 0, :8].float()
+    s = torch.zeros(8, device=dev)
+    errs = 0.0
+    outs = []
+    for tt in range(T):
+        s = ref_ch[0][tt] * s + ref_ch[1][tt]
+        outs.append(s)
+    ref = torch.stack(outs)
+    errs = float((E[0, :, 0, :8].float() - ref).norm() / ref.norm())
+
+    # e2e through the public API with pinned host buffers
+    e2e = None
+    extra = {}
+    if rank == 0 or ws > 1:
+        hA = A.cpu().pin_memory()
+        hB = B.cpu().pin_memory()
+        hE = torch.empty_like(hA).pin_memory()
+        dA = torch.empty_like(A)
+        dB = torch.empty_like(B)
+        k2 = max(3, min(args.steps, 10))
+
+        def e2e_step():
+            dA.copy_(hA, non_blocking=True)
+            dB.copy_(hB, non_blocking=True)
+            out = thunder_scan(dA, dB, compass=16)
+            hE.copy_(out, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k2):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / k2
+        tt_ = torch.tensor([ms], device=dev, dtype=torch.float64)
+        if ws > 1:
+            dist.all_reduce(tt_, op=dist.ReduceOp.MAX)
+        ms = float(tt_.item())
+        e2e = {"value": ws * alg_bytes / (ms * 1e-3) / 1e9, "unit": UNIT,
+               "h2d_bytes_per_step": 2 * N * 2, "d2h_bytes_per_step": N * 2,
+               "ms_per_step": ms, "api": "esa.backends.thunder.thunder_scan, pinned host buffers"}
+        del hA, hB, hE, dA, dB
+
+        # secondary figures: reverse scan fp16 and forward fp32 (kernel-only)
+        if not args.quick:
+            extra = secondary(dev, stream, L, args)
+
+    if ws > 1:
+        barrier()
+
+    if rank == 0:
+        traffic = _traffic_summary()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded)",
+            "config": {"workload": WORKLOAD, "shape_BTHD": list(SHAPE), "compass": compass,
+                       "parallelism": f"batch x head sharding, {ws} independent shards",
+                       "l2": "inputs 537 MB + output 268 MB > 126 MB L2; no flush",
+                       "spot_check_rel_err": errs},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": alg_bytes,
+                         "mean_launch_ms": mean_launch_ms,
+                         "kernel": "tiled_scan_kernel<FwdPlain, half, half>",
+                         "traffic": (traffic or {}).get("bytes_per_launch"),
+                         "traffic_source": (traffic or {}).get("source")},
+            "cpu_baseline": None,
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": clk,
+        }
+        if extra:
+            line["secondary"] = extra
+        if ws == 1 and not args.no_cpu:
+            try:
+                line["cpu_baseline"] = cpu_baseline()
+            except Exception as exc:  # the CPU baseline never blocks the GPU line
+                line["cpu_baseline"] = {"error": str(exc)}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
+
+
+def secondary(dev, stream, L, args) -> dict:
+    import torch
+
+    from esa import _lib
+
+    nb, T, H, D = SHAPE
+    hd = H * D
+    N = nb * T * hd
+    out = {}
+    sp = stream.cuda_stream
+
+    def timeit(fn, k=30):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(k):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / k
+
+    g = torch.Generator(device=dev).manual_seed(99)
+    for name, dt, code, es in (("fwd_f32", torch.float32, _lib.DTYPE_F32, 4),):
+        A = torch.sigmoid(torch.randn(SHAPE, device=dev, generator=g) * 2 + 2).to(dt)
+        B = torch.randn(SHAPE, device=dev, generator=g).to(dt)
+        E = torch.empty_like(A)
+        for compass in (16, 32, 64):
+            wsb = L.esa_scan_workspace_bytes(nb, T, hd, code, compass)
+            w = torch.empty(wsb, dtype=torch.uint8, device=dev)
+            ms = timeit(lambda: L.esa_scan_fwd(A.data_ptr(), B.data_ptr(), E.data_ptr(), nb, T, hd,
+                                               code, compass, None, None, w.data_ptr(), wsb, sp))
+            out[f"{name}_c{compass}_GBps"] = 3 * N * es / (ms * 1e-3) / 1e9
+        del A, B, E
+    A = torch.sigmoid(torch.randn(SHAPE, device=dev, generator=g) * 2 + 2).half()
+    B = torch.randn(SHAPE, device=dev, generator=g).half()
+    E = torch.empty_like(A)
+    for compass in (32, 64):
+        wsb = L.esa_scan_workspace_bytes(nb, T, hd, _lib.DTYPE_F16, compass)
+        w = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        ms = timeit(lambda: L.esa_scan_fwd(A.data_ptr(), B.data_ptr(), E.data_ptr(), nb, T, hd,
+                                           _lib.DTYPE_F16, compass, None, None, w.data_ptr(), wsb, sp))
+        out[f"fwd_f16_c{compass}_GBps"] = 3 * N * 2 / (ms * 1e-3) / 1e9
+    dE = torch.randn(SHAPE, device=dev, generator=g).half()
+    dA = torch.empty_like(A)
+    dB = torch.empty_like(A)
+    wsb = L.esa_scan_workspace_bytes(nb, T, hd, _lib.DTYPE_F16, 16)
+    w = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    ms = timeit(lambda: L.esa_scan_rev(A.data_ptr(), E.data_ptr(), dE.data_ptr(), dA.data_ptr(),
+                                       dB.data_ptr(), nb, T, hd, _lib.DTYPE_F16, 16, None, None,
+                                       w.data_ptr(), wsb, sp))
+    out["rev_f16_c16_GBps"] = 5 * N * 2 / (ms * 1e-3) / 1e9
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--quick", action="store_true", help="skip the secondary figures")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,105 @@
+// esa_capi.cu -- the extern "C" entry points declared in include/esa_b200.h.
+//
+// Thin wrappers: argument checks that need no device work, the thread-local
+// last-error string, and dispatch to the kernels' host launchers.
+#include <mutex>
+#include <string>
+
+#include "../../include/esa_b200.h"
+#include "esa_internal.h"
+
+namespace esa {
+
+static thread_local std::string t_last_error;
+
+int set_error(int code, const std::string& msg) {
+    t_last_error = msg;
+    return code;
+}
+
+void clear_error() { t_last_error.clear(); }
+
+int device_sm_count(int device) {
+    static int cache[64] = {0};
+    static std::mutex mu;
+    if (device < 0 || device >= 64) return 148;
+    std::lock_guard<std::mutex> lock(mu);
+    if (cache[device] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+            n = 148;
+        cache[device] = n;
+    }
+    return cache[device];
+}
+
+}  // namespace esa
+
+using namespace esa;
+
+extern "C" {
+
+int esa_abi_version(void) { return ESA_ABI_VERSION; }
+
+const char* esa_last_error(void) { return t_last_error.c_str(); }
+
+int esa_device_status(int device, int clear, unsigned int* status) {
+    clear_error();
+    if (status == nullptr) return set_error(ESA_ERR_INVALID_ARGUMENT, "status pointer is null");
+    return device_status(device, clear, status);
+}
+
+size_t esa_scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int dtype, int compass) {
+    const int es = dtype_size(dtype);
+    if (es == 0 || nb < 0 || T < 0 || hd < 0 || compass <= 0) return 0;
+    return scan_workspace_bytes(nb, T, hd, es, compass);
+}
+
+int esa_scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd,
+                 int dtype, int compass, const void* e0, void* e_last, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+    clear_error();
+    return scan_fwd(A, B, E, nb, T, hd, dtype, compass, e0, e_last, workspace, workspace_bytes,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int esa_scan_rev(const void* A, const void* E, const void* dE, void* dA, void* dB, int64_t nb,
+                 int64_t T, int64_t hd, int dtype, int compass, const void* e0, void* de0,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    return scan_rev(A, E, dE, dA, dB, nb, T, hd, dtype, compass, e0, de0, workspace,
+                    workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int esa_gated_scan_fwd(const void* gate_raw, const void* value_raw, int64_t raw_row_stride,
+                       int raw_dtype, void* E, int e_dtype, int64_t nb, int64_t T, int64_t hd,
+                       float gate_min, float gate_max, int round_ab, int compass, const void* e0,
+                       void* e_last, void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    return gated_scan_fwd(gate_raw, value_raw, raw_row_stride, raw_dtype, E, e_dtype, nb, T, hd,
+                          gate_min, gate_max, round_ab, compass, e0, e_last, workspace,
+                          workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int esa_gated_scan_bwd(const void* gate_raw, const void* value_raw, int64_t raw_row_stride,
+                       int raw_dtype, const void* E, const void* dE, int e_dtype,
+                       void* d_gate_raw, void* d_value_raw, int64_t draw_row_stride,
+                       int draw_dtype, int64_t nb, int64_t T, int64_t hd, float gate_min,
+                       float gate_max, int round_ab, int compass, const void* e0, void* de0,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    return gated_scan_bwd(gate_raw, value_raw, raw_row_stride, raw_dtype, E, dE, e_dtype,
+                          d_gate_raw, d_value_raw, draw_row_stride, draw_dtype, nb, T, hd,
+                          gate_min, gate_max, round_ab, compass, e0, de0, workspace,
+                          workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int esa_lightning_step(const void* qgv, int64_t qgv_row_stride, int qgv_dtype, const void* state,
+                       void* new_state, int state_dtype, void* z, int z_dtype, int64_t nb,
+                       int64_t C, float gate_min, float gate_max, float eps, void* stream) {
+    clear_error();
+    return lightning_step(qgv, qgv_row_stride, qgv_dtype, state, new_state, state_dtype, z, z_dtype,
+                          nb, C, gate_min, gate_max, eps, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

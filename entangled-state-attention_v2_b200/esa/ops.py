@@ -1,0 +1,335 @@
+"""PyTorch operators over the C-ABI library (``libesa_b200.so``).
+
+Each operator is a ``torch.library.custom_op`` with a fake (meta) kernel and,
+where the reference path is differentiable, an autograd formula, so that it is
+opaque to ``torch.compile`` (no graph break inside) and capturable in CUDA
+graphs (fixed workspace, no host synchronisation).  Work is enqueued on the
+current CUDA stream.  CPU tensors raise: there is no CPU fallback.
+
+Operators
+---------
+``esa_b200::scan``                 E, e_last = scan(A, B, e0)         (kernel a)
+``esa_b200::scan_backward``        dA, dB, de0                        (kernel b, bare)
+``esa_b200::gated_scan``           E, e_last from gate/value logits   (kernel a + gate prologue)
+``esa_b200::gated_scan_backward``  d gate, d value, de0               (kernel b + gate epilogue)
+``esa_b200::lightning_step``       new state, out_proj input          (kernel c)
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+_CODES = {
+    torch.float16: _lib.DTYPE_F16,
+    torch.bfloat16: _lib.DTYPE_BF16,
+    torch.float32: _lib.DTYPE_F32,
+    torch.float64: _lib.DTYPE_F64,
+}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _CODES[dt]
+    except KeyError:
+        raise TypeError(f"ESA kernels support float16/bfloat16/float32/float64, got {dt}") from None
+
+
+def acc_dtype(*dts: torch.dtype) -> torch.dtype:
+    return torch.float64 if torch.float64 in dts else torch.float32
+
+
+def _widest(*dts: torch.dtype) -> torch.dtype:
+    return max(dts, key=lambda d: (torch.empty((), dtype=d).element_size(), d == torch.float64))
+
+
+def _require_cuda(who: str, *ts: Optional[Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                f"{who}: the ESA B200 kernels need CUDA tensors (there is no CPU fallback); "
+                f"got a tensor on {t.device}"
+            )
+
+
+def _stream(t: Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: Optional[Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _workspace(nb: int, T: int, hd: int, dt: torch.dtype, compass: int, device) -> Tensor:
+    n = _lib.lib().esa_scan_workspace_bytes(nb, T, hd, dtype_code(dt), int(compass))
+    if n == 0 and nb * T * hd > 0:
+        raise ValueError("invalid scan problem")
+    return torch.empty(max(int(n), 256), dtype=torch.uint8, device=device)
+
+
+def _rows(t: Tensor) -> tuple[Tensor, int]:
+    """A [B, T, C] view with unit channel stride and uniformly spaced (b, t)
+    rows, and its row stride in elements (copies the tensor if it is not)."""
+    B, T, C = t.shape
+    s0, s1, s2 = t.stride()
+    if s2 == 1 and (B <= 1 or s0 == T * s1) and s1 >= C:
+        return t, (s1 if T > 1 else (s0 if B > 1 else C))
+    t = t.contiguous()
+    return t, C
+
+
+def _state_arg(e0: Optional[Tensor], nb: int, hd: int, acc: torch.dtype) -> Optional[Tensor]:
+    if e0 is None:
+        return None
+    return e0.reshape(nb, hd).to(acc).contiguous()
+
+
+# --------------------------------------------------------------------------
+# Forward / reverse scan over materialised A, B  (thunder_scan, pulse_scan)
+# --------------------------------------------------------------------------
+@torch.library.custom_op("esa_b200::scan", mutates_args=())
+def scan(A: Tensor, B: Tensor, e0: Optional[Tensor], compass: int) -> tuple[Tensor, Tensor]:
+    """E_t = A_t E_{t-1} + B_t over [B,T,H,D]; returns (E, E_{T-1} in the acc dtype)."""
+    _require_cuda("esa scan", A, B, e0)
+    nb, T, H, D = A.shape
+    hd = H * D
+    A = A.contiguous()
+    B = B.contiguous()
+    acc = acc_dtype(A.dtype)
+    E = torch.empty_like(A)
+    e0c = _state_arg(e0, nb, hd, acc)
+    if T == 0 or nb * hd == 0:
+        e_last = e0c.clone() if e0c is not None else A.new_zeros(nb, hd, dtype=acc)
+        return E, e_last
+    e_last = torch.empty(nb, hd, dtype=acc, device=A.device)
+    ws = _workspace(nb, T, hd, A.dtype, compass, A.device)
+    rc = _lib.lib().esa_scan_fwd(A.data_ptr(), B.data_ptr(), E.data_ptr(), nb, T, hd,
+                                 dtype_code(A.dtype), int(compass), _ptr(e0c), e_last.data_ptr(),
+                                 ws.data_ptr(), ws.numel(), _stream(A))
+    _lib.check(rc, "esa_scan_fwd")
+    return E, e_last
+
+
+@scan.register_fake
+def _(A, B, e0, compass):
+    nb, T, H, D = A.shape
+    return torch.empty_like(A, memory_format=torch.contiguous_format), \
+        A.new_empty(nb, H * D, dtype=acc_dtype(A.dtype))
+
+
+@torch.library.custom_op("esa_b200::scan_backward", mutates_args=())
+def scan_backward(A: Tensor, E: Tensor, dE: Tensor, e0: Optional[Tensor],
+                  compass: int) -> tuple[Tensor, Tensor, Tensor]:
+    """Reverse scan: (dA, dB, de0) for upstream gradient dE (kernel b, bare)."""
+    _require_cuda("esa scan backward", A, E, dE, e0)
+    nb, T, H, D = A.shape
+    hd = H * D
+    A, E, dE = A.contiguous(), E.contiguous(), dE.to(A.dtype).contiguous()
+    acc = acc_dtype(A.dtype)
+    dA = torch.empty_like(A)
+    dB = torch.empty_like(A)
+    de0 = torch.zeros(nb, hd, dtype=acc, device=A.device)
+    if T == 0 or nb * hd == 0:
+        return dA, dB, de0
+    e0c = _state_arg(e0, nb, hd, acc)
+    ws = _workspace(nb, T, hd, A.dtype, compass, A.device)
+    rc = _lib.lib().esa_scan_rev(A.data_ptr(), E.data_ptr(), dE.data_ptr(), dA.data_ptr(),
+                                 dB.data_ptr(), nb, T, hd, dtype_code(A.dtype), int(compass),
+                                 _ptr(e0c), de0.data_ptr(), ws.data_ptr(), ws.numel(), _stream(A))
+    _lib.check(rc, "esa_scan_rev")
+    return dA, dB, de0
+
+
+@scan_backward.register_fake
+def _(A, E, dE, e0, compass):
+    nb, T, H, D = A.shape
+    c = torch.contiguous_format
+    return (torch.empty_like(A, memory_format=c), torch.empty_like(A, memory_format=c),
+            A.new_empty(nb, H * D, dtype=acc_dtype(A.dtype)))
+
+
+def _scan_setup(ctx, inputs, output):
+    A, B, e0, compass = inputs
+    E, _ = output
+    ctx.save_for_backward(A, E, e0)
+    ctx.compass = compass
+    ctx.has_e0 = e0 is not None
+    ctx.e0_dtype = None if e0 is None else e0.dtype
+    ctx.b_dtype = B.dtype
+
+
+def _scan_bwd(ctx, dE, de_last):
+    A, E, e0 = ctx.saved_tensors
+    if dE is None:
+        dE = torch.zeros_like(E)
+    if de_last is not None:
+        dE = dE.clone()
+        dE[:, -1] += de_last.reshape(dE[:, -1].shape).to(dE.dtype)
+    dA, dB, de0 = scan_backward(A, E, dE, e0, ctx.compass)
+    return (dA, dB.to(ctx.b_dtype),
+            de0.reshape(e0.shape).to(ctx.e0_dtype) if ctx.has_e0 else None, None)
+
+
+torch.library.register_autograd("esa_b200::scan", _scan_bwd, setup_context=_scan_setup)
+
+
+# --------------------------------------------------------------------------
+# Gated scan: gate prologue fused into the forward, gate epilogue fused into
+# the reverse scan (ThunderESA.forward, esa_prefill)
+# --------------------------------------------------------------------------
+@torch.library.custom_op("esa_b200::gated_scan", mutates_args=())
+def gated_scan(gate_raw: Tensor, value_raw: Tensor, e0: Optional[Tensor], gate_min: float,
+               gate_max: float, compass: int, scan_dtype: torch.dtype) -> tuple[Tensor, Tensor]:
+    """E [B,T,C] in scan_dtype from gate/value logits [B,T,C] (row-strided views
+    allowed); returns (E, E_{T-1} in the acc dtype)."""
+    _require_cuda("esa gated scan", gate_raw, value_raw, e0)
+    if gate_raw.shape != value_raw.shape or gate_raw.dim() != 3:
+        raise ValueError(f"gate/value logits must be the same [B,T,C], got {tuple(gate_raw.shape)} "
+                         f"and {tuple(value_raw.shape)}")
+    if gate_raw.dtype != value_raw.dtype:
+        raise TypeError("gate/value logits must share a dtype")
+    nb, T, C = gate_raw.shape
+    g, rs_g = _rows(gate_raw)
+    v, rs_v = _rows(value_raw)
+    if rs_g != rs_v:
+        g, v = g.contiguous(), v.contiguous()
+        rs_g = rs_v = C
+    # the kernels accumulate in fp64 when any operand is fp64
+    acc = acc_dtype(scan_dtype, g.dtype)
+    E = torch.empty(nb, T, C, dtype=scan_dtype, device=gate_raw.device)
+    e0c = _state_arg(e0, nb, C, acc)
+    if T == 0 or nb * C == 0:
+        e_last = e0c.clone() if e0c is not None else E.new_zeros(nb, C, dtype=acc)
+        return E, e_last
+    e_last = torch.empty(nb, C, dtype=acc, device=E.device)
+    ws = _workspace(nb, T, C, _widest(g.dtype, scan_dtype), compass, E.device)
+    rc = _lib.lib().esa_gated_scan_fwd(g.data_ptr(), v.data_ptr(), rs_g, dtype_code(g.dtype),
+                                       E.data_ptr(), dtype_code(scan_dtype), nb, T, C,
+                                       float(gate_min), float(gate_max), 1, int(compass), _ptr(e0c),
+                                       e_last.data_ptr(), ws.data_ptr(), ws.numel(), _stream(E))
+    _lib.check(rc, "esa_gated_scan_fwd")
+    return E, e_last
+
+
+@gated_scan.register_fake
+def _(gate_raw, value_raw, e0, gate_min, gate_max, compass, scan_dtype):
+    nb, T, C = gate_raw.shape
+    return (gate_raw.new_empty(nb, T, C, dtype=scan_dtype),
+            gate_raw.new_empty(nb, C, dtype=acc_dtype(scan_dtype, gate_raw.dtype)))
+
+
+@torch.library.custom_op("esa_b200::gated_scan_backward", mutates_args=())
+def gated_scan_backward(gate_raw: Tensor, value_raw: Tensor, E: Tensor, dE: Tensor,
+                        e0: Optional[Tensor], gate_min: float, gate_max: float,
+                        compass: int) -> tuple[Tensor, Tensor, Tensor]:
+    """(d gate_raw, d value_raw, de0) -- reverse scan with the gate chain rule fused."""
+    _require_cuda("esa gated scan backward", gate_raw, value_raw, E, dE, e0)
+    nb, T, C = gate_raw.shape
+    g, rs_g = _rows(gate_raw)
+    v, rs_v = _rows(value_raw)
+    if rs_g != rs_v:
+        g, v = g.contiguous(), v.contiguous()
+        rs_g = C
+    E = E.contiguous()
+    dE = dE.to(E.dtype).contiguous()
+    acc = acc_dtype(E.dtype, g.dtype)
+    dg = torch.empty(nb, T, C, dtype=g.dtype, device=g.device)
+    dv = torch.empty(nb, T, C, dtype=g.dtype, device=g.device)
+    de0 = torch.zeros(nb, C, dtype=acc, device=g.device)
+    if T == 0 or nb * C == 0:
+        return dg, dv, de0
+    e0c = _state_arg(e0, nb, C, acc)
+    ws = _workspace(nb, T, C, _widest(g.dtype, E.dtype), compass, g.device)
+    rc = _lib.lib().esa_gated_scan_bwd(g.data_ptr(), v.data_ptr(), rs_g, dtype_code(g.dtype),
+                                       E.data_ptr(), dE.data_ptr(), dtype_code(E.dtype),
+                                       dg.data_ptr(), dv.data_ptr(), C, dtype_code(g.dtype),
+                                       nb, T, C, float(gate_min), float(gate_max), 1, int(compass),
+                                       _ptr(e0c), de0.data_ptr(), ws.data_ptr(), ws.numel(),
+                                       _stream(g))
+    _lib.check(rc, "esa_gated_scan_bwd")
+    return dg, dv, de0
+
+
+@gated_scan_backward.register_fake
+def _(gate_raw, value_raw, E, dE, e0, gate_min, gate_max, compass):
+    nb, T, C = gate_raw.shape
+    return (gate_raw.new_empty(nb, T, C), gate_raw.new_empty(nb, T, C),
+            gate_raw.new_empty(nb, C, dtype=acc_dtype(E.dtype, gate_raw.dtype)))
+
+
+def _gated_setup(ctx, inputs, output):
+    g, v, e0, gmin, gmax, compass, scan_dtype = inputs
+    E, _ = output
+    ctx.save_for_backward(g, v, E, e0)
+    ctx.args = (gmin, gmax, compass)
+    ctx.has_e0 = e0 is not None
+    ctx.e0_dtype = None if e0 is None else e0.dtype
+
+
+def _gated_bwd(ctx, dE, de_last):
+    g, v, E, e0 = ctx.saved_tensors
+    if dE is None:
+        dE = torch.zeros_like(E)
+    if de_last is not None:
+        dE = dE.clone()
+        dE[:, -1] += de_last.to(dE.dtype)
+    dg, dv, de0 = gated_scan_backward(g, v, E, dE, e0, *ctx.args)
+    return (dg, dv, de0.reshape(e0.shape).to(ctx.e0_dtype) if ctx.has_e0 else None,
+            None, None, None, None)
+
+
+torch.library.register_autograd("esa_b200::gated_scan", _gated_bwd, setup_context=_gated_setup)
+
+
+# --------------------------------------------------------------------------
+# ESA-Lightning one-token step (kernel c)
+# --------------------------------------------------------------------------
+@torch.library.custom_op("esa_b200::lightning_step", mutates_args=())
+def lightning_step(qgv: Tensor, state: Tensor, gate_min: float, gate_max: float, eps: float,
+                   z_dtype: torch.dtype) -> tuple[Tensor, Tensor]:
+    """qgv [B, 3C], state [B, C] -> (new_state [B, C] in state's dtype,
+    z = sigmoid(q) * S' * rsqrt(mean(S'^2) + eps) [B, C] in z_dtype)."""
+    _require_cuda("esa lightning step", qgv, state)
+    nb, c3 = qgv.shape
+    C = c3 // 3
+    if qgv.stride(1) != 1:
+        qgv = qgv.contiguous()
+    state = state.reshape(nb, C).contiguous()
+    new_state = torch.empty_like(state)
+    z = torch.empty(nb, C, dtype=z_dtype, device=qgv.device)
+    if nb == 0:
+        return new_state, z
+    rc = _lib.lib().esa_lightning_step(qgv.data_ptr(), qgv.stride(0) if nb > 1 else c3,
+                                       dtype_code(qgv.dtype), state.data_ptr(),
+                                       new_state.data_ptr(), dtype_code(state.dtype), z.data_ptr(),
+                                       dtype_code(z_dtype), nb, C, float(gate_min),
+                                       float(gate_max), float(eps), _stream(qgv))
+    _lib.check(rc, "esa_lightning_step")
+    return new_state, z
+
+
+@lightning_step.register_fake
+def _(qgv, state, gate_min, gate_max, eps, z_dtype):
+    nb, c3 = qgv.shape
+    return (state.new_empty(nb, c3 // 3), qgv.new_empty(nb, c3 // 3, dtype=z_dtype))
+
+
+def check_device_status(device=None) -> None:
+    """Raise if a kernel on `device` reported a bounded wait that ran out."""
+    if device is None:
+        device = torch.cuda.current_device()
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _lib.device_status(idx, clear=True)
+    if st:
+        names = []
+        if st & _lib.STATUS_LOOKBACK_TIMEOUT:
+            names.append("lookback wait ran out")
+        if st & _lib.STATUS_COPY_TIMEOUT:
+            names.append("bulk copy wait ran out")
+        raise RuntimeError(f"ESA kernel on cuda:{idx} reported: {', '.join(names)} "
+                           f"(status {st:#x}); results of the affected launch are invalid")

@@ -1,0 +1,138 @@
+/*
+ * esa_b200.h -- C ABI of the B200 (sm_100a) ESA recurrence library
+ * (libesa_b200.so).
+ *
+ * The reference (maxzameer/Entangled-State-Attention_v2 v2.1.1) is a pure
+ * Python/PyTorch package with no FFI of its own; these entry points are the
+ * functions its Python hot path would bind.  Each declaration cites the
+ * reference interface it replaces.
+ *
+ * Conventions
+ *   - All pointers are device pointers (cudaMalloc / PyTorch CUDA tensors),
+ *     except where noted.  The library never allocates or frees memory, never
+ *     synchronises the host and enqueues all work on `stream` (a cudaStream_t
+ *     passed as void*; NULL = legacy default stream).
+ *   - Tensors of shape [B, T, H, D] are passed as (nb = B, T, hd = H*D) and are
+ *     contiguous with hd the fastest axis, the reference's layout
+ *     (esa/backends/thunder.py:97-110).
+ *   - Return value: ESA_OK (0) or a negative ESA_ERR_* code; esa_last_error()
+ *     gives a message (thread-local).  Failures detected on the device (a wait
+ *     that ran past its one-second budget) are OR-ed into a per-device status
+ *     word read by esa_device_status().
+ *   - "acc" type: float for f16/bf16/f32 data, double for f64 data.  Initial
+ *     and final states (e0, e_last, de0) use the acc type, shape [nb, hd].
+ */
+#ifndef ESA_B200_H
+#define ESA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element type codes */
+#define ESA_DTYPE_F16 0
+#define ESA_DTYPE_BF16 1
+#define ESA_DTYPE_F32 2
+#define ESA_DTYPE_F64 3
+
+/* return codes */
+#define ESA_OK 0
+#define ESA_ERR_INVALID_ARGUMENT (-1)
+#define ESA_ERR_UNSUPPORTED_DTYPE (-2)
+#define ESA_ERR_WORKSPACE (-3)
+#define ESA_ERR_CUDA (-4)
+
+/* device status bits */
+#define ESA_STATUS_LOOKBACK_TIMEOUT 1u
+#define ESA_STATUS_COPY_TIMEOUT 2u
+
+#define ESA_ABI_VERSION 1
+
+/* Version of this ABI (ESA_ABI_VERSION). */
+int esa_abi_version(void);
+
+/* Message for the last failing call on this host thread ("" if none). */
+const char *esa_last_error(void);
+
+/* Reads the device status word of `device` into *status (host pointer);
+ * clears it when `clear` is non-zero.  Synchronises that device.
+ * Replaces nothing in the reference (it has no device code); it is how the
+ * bounded waits of the scans report failure. */
+int esa_device_status(int device, int clear, unsigned int *status);
+
+/* Workspace bytes a scan call needs for this problem (lookback descriptors and
+ * flags).  0 is never returned for a valid problem.  `compass` as in
+ * esa_scan_fwd. */
+size_t esa_scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int dtype, int compass);
+
+/* Forward recurrence E_t = A_t * E_{t-1} + B_t, E_{-1} = e0 (NULL: zero).
+ * A, B, E: [nb, T, hd] of `dtype`; accumulation in the acc type.
+ * e_last (nullable): receives E_{T-1} in the acc type.
+ * compass: the reference's Thunder chunk size (any positive int); here it
+ * selects the time extent of one CTA tile (16, 32 or 64 steps, nearest) and
+ * does not change results beyond fp32 summation order.
+ * Replaces thunder_scan(A, B_write, compass) -- esa/backends/thunder.py:70-159
+ * (and pulse_scan, esa/backends/pulse.py:12-31). */
+int esa_scan_fwd(const void *A, const void *B, void *E, int64_t nb, int64_t T, int64_t hd,
+                 int dtype, int compass, const void *e0, void *e_last, void *workspace,
+                 size_t workspace_bytes, void *stream);
+
+/* Reverse-time scan: the gradient of esa_scan_fwd.
+ *   G_t = dE_t + A_{t+1} G_{t+1};  dB_t = G_t;  dA_t = G_t * E_{t-1}
+ * with E_{-1} = e0 (NULL: zero); de0 (nullable) receives A_0 * G_0, the
+ * gradient w.r.t. e0, in the acc type.  All tensors [nb, T, hd] of `dtype`.
+ * Replaces the autograd backward of thunder_scan (esa/backends/thunder.py:
+ * 70-159 has none of its own); math of esa/backends/flare.py:49-78. */
+int esa_scan_rev(const void *A, const void *E, const void *dE, void *dA, void *dB, int64_t nb,
+                 int64_t T, int64_t hd, int dtype, int compass, const void *e0, void *de0,
+                 void *workspace, size_t workspace_bytes, void *stream);
+
+/* Forward scan with the gate prologue fused in.  gate_raw / value_raw are
+ * row-strided views ([nb, T] rows of hd elements, `raw_row_stride` elements
+ * apart -- e.g. 3*C for the gate and value slices of a qgv [B,T,3C] tensor)
+ * of `raw_dtype`.  Per element:
+ *   A = gmin + (gmax - gmin) * sigmoid(gate_raw),  B = (1 - A) * tanh(value_raw)
+ * both rounded to `e_dtype` first when round_ab != 0 (the reference's
+ * A.to(scan_dtype)), then E_t = A_t E_{t-1} + B_t written as `e_dtype`.
+ * Replaces esa/backends/thunder.py:282-302 (ThunderESA.forward: gate, cast,
+ * thunder_scan) and generation.py:439-445 + :476-487 (prefill). */
+int esa_gated_scan_fwd(const void *gate_raw, const void *value_raw, int64_t raw_row_stride,
+                       int raw_dtype, void *E, int e_dtype, int64_t nb, int64_t T, int64_t hd,
+                       float gate_min, float gate_max, int round_ab, int compass, const void *e0,
+                       void *e_last, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Backward of esa_gated_scan_fwd, fused: reverse scan plus the gate chain rule
+ *   dg = (dA - dB * tanh v) * (gmax - gmin) * s (1 - s),  s = sigmoid(g)
+ *   dv = dB * (1 - A) * (1 - tanh^2 v)
+ * writing d_gate_raw / d_value_raw as row-strided views (`draw_row_stride`,
+ * `draw_dtype`, e.g. slices of the qgv gradient).  E and dE: [nb, T, hd] of
+ * e_dtype.  A is recomputed from gate_raw exactly as the forward did.
+ * Replaces the autograd of thunder.py:282-302. */
+int esa_gated_scan_bwd(const void *gate_raw, const void *value_raw, int64_t raw_row_stride,
+                       int raw_dtype, const void *E, const void *dE, int e_dtype,
+                       void *d_gate_raw, void *d_value_raw, int64_t draw_row_stride,
+                       int draw_dtype, int64_t nb, int64_t T, int64_t hd, float gate_min,
+                       float gate_max, int round_ab, int compass, const void *e0, void *de0,
+                       void *workspace, size_t workspace_bytes, void *stream);
+
+/* One ESA-Lightning decode step for nb rows, fused: gate nonlinearity, state
+ * update and the RMS readout over all C = H*D channels.
+ *   qgv: [nb, 3C] rows `qgv_row_stride` elements apart (q | gate | value)
+ *   state -> new_state: [nb, C] of state_dtype (may alias)
+ *   z: [nb, C] of z_dtype, z = sigmoid(q) * S' * rsqrt(mean(S'^2) + eps),
+ *      the input of out_proj.
+ * Replaces esa/generation.py:443-458 (lightning_decode_step: gates, S' =
+ * A S + B, _readout up to out_proj; _readout is generation.py:270-293). */
+int esa_lightning_step(const void *qgv, int64_t qgv_row_stride, int qgv_dtype,
+                       const void *state, void *new_state, int state_dtype, void *z,
+                       int z_dtype, int64_t nb, int64_t C, float gate_min, float gate_max,
+                       float eps, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ESA_B200_H */

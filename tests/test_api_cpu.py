@@ -1,0 +1,179 @@
+"""CPU-side checks: the drop-in API surface, argument validation, the C ABI
+library (loads and exports every symbol include/esa_b200.h declares, without
+calling compute), and that the product has no CPU fallback."""
+import ctypes
+import inspect
+import re
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+HEADER = ROOT / "include" / "esa_b200.h"
+
+
+def _declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(esa_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_abi():
+    syms = _declared_symbols()
+    assert set(syms) == {
+        "esa_abi_version", "esa_last_error", "esa_device_status", "esa_scan_workspace_bytes",
+        "esa_scan_fwd", "esa_scan_rev", "esa_gated_scan_fwd", "esa_gated_scan_bwd",
+        "esa_lightning_step"}
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    from esa import _lib
+    L = _lib.lib()
+    for name in _declared_symbols():
+        assert hasattr(L, name), name
+        assert name in _lib.SIGNATURES, name
+    assert L.esa_abi_version() == _lib.ABI_VERSION
+    assert _lib.last_error() == ""
+
+
+def test_workspace_size_is_pure_host_arithmetic():
+    from esa import _lib
+    L = _lib.lib()
+    n16 = L.esa_scan_workspace_bytes(32, 4096, 1024, _lib.DTYPE_F16, 16)
+    n32 = L.esa_scan_workspace_bytes(32, 4096, 1024, _lib.DTYPE_F32, 16)
+    assert n16 > 0 and n32 > 0
+    assert L.esa_scan_workspace_bytes(32, 4096, 1024, 9, 16) == 0      # bad dtype
+    assert L.esa_scan_workspace_bytes(32, 4096, 1024, _lib.DTYPE_F16, 0) == 0  # bad compass
+
+
+def test_abi_argument_errors_need_no_gpu():
+    from esa import _lib
+    L = _lib.lib()
+    rc = L.esa_scan_fwd(None, None, None, 1, 4, 8, _lib.DTYPE_F32, 0, None, None, None, 0, None)
+    assert rc == -1 and "compass" in _lib.last_error()
+    rc = L.esa_scan_fwd(None, None, None, 1, 4, 8, 7, 16, None, None, None, 0, None)
+    assert rc in (-1, -2)
+    rc = L.esa_lightning_step(None, 3, _lib.DTYPE_F32, None, None, _lib.DTYPE_F32, None,
+                              _lib.DTYPE_F32, 1, 4, 0.8, 0.995, 1e-5, None)
+    assert rc == -1 and "stride" in _lib.last_error()
+
+
+def test_public_surface_matches_reference():
+    import esa
+    from esa import ESA
+    from esa.backends import FlareESA, PulseESA, ThunderESA, flare_scan, pulse_scan, thunder_scan
+    from esa.generation import (esa_prefill, lightning_decode_step, lightning_init_state,
+                                lightning_prefill, parse_engine_spec, sample_next_token)
+    assert esa.__version__ == "2.1.1"
+    sig = inspect.signature(ESA)
+    assert sig.parameters["backend"].default == "thunder"
+    assert sig.parameters["precision"].default == "fp16"
+    assert sig.parameters["eps"].default == 1e-5
+    assert list(inspect.signature(thunder_scan).parameters) == ["A", "B_write", "compass", "c"]
+    assert inspect.signature(thunder_scan).parameters["compass"].default == 16
+    assert lightning_prefill is esa_prefill
+    del FlareESA, PulseESA, ThunderESA, flare_scan, pulse_scan, lightning_decode_step
+    del lightning_init_state, parse_engine_spec, sample_next_token
+
+
+def test_layer_validation_matches_reference():
+    from esa import ESA
+    layer = ESA(embd=32, head=4, device=None)
+    assert layer.compass == 16 and layer.backend == "thunder"
+    assert ESA(embd=32, head=4, backend="pulse", device=None).compass is None
+    with pytest.raises(ValueError, match="compass is only supported"):
+        ESA(embd=32, head=4, backend="pulse", compass=16, device=None)
+    with pytest.raises(ValueError, match="compass is only supported"):
+        ESA(embd=32, head=4, backend="flare", compass=16, device=None)
+    with pytest.raises(TypeError):
+        ESA(n_embd=32, n_head=4)
+    with pytest.raises(ValueError, match="Supported backends"):
+        ESA(embd=32, head=4, backend="lightning", device=None)
+    with pytest.raises(ValueError, match="divisible"):
+        ESA(embd=30, head=4, device=None)
+    with pytest.raises(ValueError, match="compass must be positive"):
+        ESA(embd=32, head=4, compass=-1, device=None)
+
+
+def test_state_dict_keys_match_reference_checkpoint():
+    import numpy as np
+    from conftest import GOLDEN
+    from esa import ESAModel, ESAModelConfig
+    z = np.load(GOLDEN / "model_generate.npz")
+    ref_keys = {k[4:] for k in z.files if k.startswith("sd::")}
+    cfg = ESAModelConfig(vocab_size=64, block=32, n_layer=2, head=4, embd=32, dropout=0.0,
+                         precision="fp32", backend="thunder")
+    model = ESAModel(cfg, device="cpu")
+    assert set(model.state_dict().keys()) == ref_keys
+    sd = {k[4:]: torch.from_numpy(z[k]) for k in z.files if k.startswith("sd::")}
+    model.load_state_dict(sd, strict=True)
+
+
+def test_engine_parser_and_precision():
+    from esa.generation import parse_engine_spec
+    from esa.precision import resolve_scan_dtype
+    s = parse_engine_spec("thunder_compiled_16")
+    assert (s.backend, s.compiled, s.compass) == ("thunder", True, 16)
+    assert parse_engine_spec("flare_compiled").compiled
+    assert parse_engine_spec("lightning").backend == "lightning"
+    assert parse_engine_spec("thunder").compass == 16
+    with pytest.raises(ValueError):
+        parse_engine_spec("pulse_16")
+    with pytest.raises(ValueError):
+        parse_engine_spec("warp")
+    assert resolve_scan_dtype("fp16", "cuda") == torch.float16
+    assert resolve_scan_dtype("fp16", "cpu") == torch.float32
+    assert resolve_scan_dtype("bf16", "cpu") == torch.bfloat16
+    assert resolve_scan_dtype("fp64", "cuda") == torch.float64
+    with pytest.warns(RuntimeWarning):
+        assert resolve_scan_dtype("fp8", "cuda") == torch.float16
+    with pytest.raises(NotImplementedError):
+        resolve_scan_dtype("fp8", "cuda", strict_precision=True)
+    with pytest.raises(ValueError):
+        resolve_scan_dtype("int8", "cuda")
+
+
+def test_no_cpu_fallback():
+    from esa import ESA
+    from esa.backends.thunder import thunder_scan
+    layer = ESA(embd=32, head=4, precision="fp32", device=None)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        layer(torch.randn(2, 16, 32))
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        thunder_scan(torch.rand(1, 4, 2, 8), torch.rand(1, 4, 2, 8))
+
+
+def test_scan_argument_errors_on_cpu_tensors():
+    from esa.backends.thunder import thunder_scan
+    a = torch.ones(2, 3, 4, 5)
+    with pytest.raises(ValueError, match="same shape"):
+        thunder_scan(a, torch.ones(2, 3, 4, 6))
+    with pytest.raises(ValueError, match=r"\[B,T,H,D\]"):
+        thunder_scan(a[0], a[0])
+    with pytest.raises(ValueError, match="positive integer"):
+        thunder_scan(a, a, compass=0)
+    with pytest.raises(ValueError, match="positive integer"):
+        thunder_scan(a, a, c=-3)
+
+
+def test_fake_kernels_trace_without_gpu():
+    """The custom ops have meta kernels: shapes/dtypes propagate on the meta device."""
+    from esa import ops
+    A = torch.empty(2, 10, 4, 8, device="meta", dtype=torch.float16)
+    E, el = ops.scan(A, A, None, 16)
+    assert E.shape == A.shape and E.dtype == torch.float16 and el.shape == (2, 32)
+    assert el.dtype == torch.float32
+    g = torch.empty(2, 10, 96, device="meta")[..., 32:64]
+    E, el = ops.gated_scan(g, g, None, 0.8, 0.995, 16, torch.bfloat16)
+    assert E.shape == (2, 10, 32) and E.dtype == torch.bfloat16
+    ns, z = ops.lightning_step(torch.empty(3, 96, device="meta"),
+                               torch.empty(3, 32, device="meta", dtype=torch.float16),
+                               0.8, 0.995, 1e-5, torch.float32)
+    assert ns.dtype == torch.float16 and z.dtype == torch.float32 and z.shape == (3, 32)
+
+
+def test_library_symbols_via_ctypes_cdll():
+    from esa import _lib
+    cdll = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in _declared_symbols():
+        getattr(cdll, name)
