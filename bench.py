@@ -264,16 +264,16 @@ def run_ours(args) -> None:
     achieved = alg_bytes / (mean_launch_ms * 1e-3) / 1e9
     ops.check_device_status(dev)
 
-    # correctness spot check of the timed output (a few channels vs fp32 torch)
-    ref_ch = A[0, :, 0, :8].float(), B[0, :, 0, :8].float()
-    s = torch.zeros(8, device=dev)
-    errs = 0.0
+    # correctness spot check of the timed output: 16 channels x the first 256
+    # steps against a plain fp32 torch recurrence
+    ref_a, ref_b = A[0, :256, 0, :16].float(), B[0, :256, 0, :16].float()
+    s = torch.zeros(16, device=dev)
     outs = []
-    for tt in range(T):
-        s = ref_ch[0][tt] * s + ref_ch[1][tt]
+    for tt in range(256):
+        s = ref_a[tt] * s + ref_b[tt]
         outs.append(s)
     ref = torch.stack(outs)
-    errs = float((E[0, :, 0, :8].float() - ref).norm() / ref.norm())
+    errs = float((E[0, :256, 0, :16].float() - ref).norm() / ref.norm())
 
     # e2e through the public API with pinned host buffers
     e2e = None

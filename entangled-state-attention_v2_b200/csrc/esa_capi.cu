@@ -37,25 +37,28 @@ int device_sm_count(int device) {
 
 using namespace esa;
 
+// the library is built with hidden visibility; only the C ABI is exported
+#define ESA_EXPORT __attribute__((visibility("default")))
+
 extern "C" {
 
-int esa_abi_version(void) { return ESA_ABI_VERSION; }
+ESA_EXPORT int esa_abi_version(void) { return ESA_ABI_VERSION; }
 
-const char* esa_last_error(void) { return t_last_error.c_str(); }
+ESA_EXPORT const char* esa_last_error(void) { return t_last_error.c_str(); }
 
-int esa_device_status(int device, int clear, unsigned int* status) {
+ESA_EXPORT int esa_device_status(int device, int clear, unsigned int* status) {
     clear_error();
     if (status == nullptr) return set_error(ESA_ERR_INVALID_ARGUMENT, "status pointer is null");
     return device_status(device, clear, status);
 }
 
-size_t esa_scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int dtype, int compass) {
+ESA_EXPORT size_t esa_scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int dtype, int compass) {
     const int es = dtype_size(dtype);
     if (es == 0 || nb < 0 || T < 0 || hd < 0 || compass <= 0) return 0;
     return scan_workspace_bytes(nb, T, hd, es, compass);
 }
 
-int esa_scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd,
+ESA_EXPORT int esa_scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd,
                  int dtype, int compass, const void* e0, void* e_last, void* workspace,
                  size_t workspace_bytes, void* stream) {
     clear_error();
@@ -63,7 +66,7 @@ int esa_scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, i
                     static_cast<cudaStream_t>(stream));
 }
 
-int esa_scan_rev(const void* A, const void* E, const void* dE, void* dA, void* dB, int64_t nb,
+ESA_EXPORT int esa_scan_rev(const void* A, const void* E, const void* dE, void* dA, void* dB, int64_t nb,
                  int64_t T, int64_t hd, int dtype, int compass, const void* e0, void* de0,
                  void* workspace, size_t workspace_bytes, void* stream) {
     clear_error();
@@ -71,9 +74,9 @@ int esa_scan_rev(const void* A, const void* E, const void* dE, void* dA, void* d
                     workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
-int esa_gated_scan_fwd(const void* gate_raw, const void* value_raw, int64_t raw_row_stride,
+ESA_EXPORT int esa_gated_scan_fwd(const void* gate_raw, const void* value_raw, int64_t raw_row_stride,
                        int raw_dtype, void* E, int e_dtype, int64_t nb, int64_t T, int64_t hd,
-                       float gate_min, float gate_max, int round_ab, int compass, const void* e0,
+                       double gate_min, double gate_max, int round_ab, int compass, const void* e0,
                        void* e_last, void* workspace, size_t workspace_bytes, void* stream) {
     clear_error();
     return gated_scan_fwd(gate_raw, value_raw, raw_row_stride, raw_dtype, E, e_dtype, nb, T, hd,
@@ -81,11 +84,11 @@ int esa_gated_scan_fwd(const void* gate_raw, const void* value_raw, int64_t raw_
                           workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
-int esa_gated_scan_bwd(const void* gate_raw, const void* value_raw, int64_t raw_row_stride,
+ESA_EXPORT int esa_gated_scan_bwd(const void* gate_raw, const void* value_raw, int64_t raw_row_stride,
                        int raw_dtype, const void* E, const void* dE, int e_dtype,
                        void* d_gate_raw, void* d_value_raw, int64_t draw_row_stride,
-                       int draw_dtype, int64_t nb, int64_t T, int64_t hd, float gate_min,
-                       float gate_max, int round_ab, int compass, const void* e0, void* de0,
+                       int draw_dtype, int64_t nb, int64_t T, int64_t hd, double gate_min,
+                       double gate_max, int round_ab, int compass, const void* e0, void* de0,
                        void* workspace, size_t workspace_bytes, void* stream) {
     clear_error();
     return gated_scan_bwd(gate_raw, value_raw, raw_row_stride, raw_dtype, E, dE, e_dtype,
@@ -94,9 +97,9 @@ int esa_gated_scan_bwd(const void* gate_raw, const void* value_raw, int64_t raw_
                           workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
-int esa_lightning_step(const void* qgv, int64_t qgv_row_stride, int qgv_dtype, const void* state,
+ESA_EXPORT int esa_lightning_step(const void* qgv, int64_t qgv_row_stride, int qgv_dtype, const void* state,
                        void* new_state, int state_dtype, void* z, int z_dtype, int64_t nb,
-                       int64_t C, float gate_min, float gate_max, float eps, void* stream) {
+                       int64_t C, double gate_min, double gate_max, double eps, void* stream) {
     clear_error();
     return lightning_step(qgv, qgv_row_stride, qgv_dtype, state, new_state, state_dtype, z, z_dtype,
                           nb, C, gate_min, gate_max, eps, static_cast<cudaStream_t>(stream));

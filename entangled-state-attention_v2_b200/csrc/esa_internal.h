@@ -1,4 +1,5 @@
-// esa_internal.h -- host-side declarations shared by the library's translation units.
+// esa_internal.h -- host-side declarations shared by the library's translation
+// units, and the plain argument structs the scan kernels receive.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -15,27 +16,9 @@ int set_error(int code, const std::string& msg);
 void clear_error();
 // Number of SMs of `device` (cached).
 int device_sm_count(int device);
-
-size_t scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int compass);
+// Device address of the status word on `device` (cached; null on failure).
+unsigned* status_ptr(int device);
 int device_status(int device, int clear, unsigned* status);
-
-int scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd, int dtype,
-             int compass, const void* e0, void* e_last, void* ws, size_t ws_bytes, cudaStream_t s);
-int scan_rev(const void* A, const void* E, const void* dE, void* dA, void* dB, int64_t nb, int64_t T,
-             int64_t hd, int dtype, int compass, const void* e0, void* de0, void* ws, size_t ws_bytes,
-             cudaStream_t s);
-int gated_scan_fwd(const void* g, const void* v, int64_t rrs, int raw_dtype, void* E, int e_dtype,
-                   int64_t nb, int64_t T, int64_t hd, float gmin, float gmax, int round_ab,
-                   int compass, const void* e0, void* e_last, void* ws, size_t ws_bytes,
-                   cudaStream_t s);
-int gated_scan_bwd(const void* g, const void* v, int64_t rrs, int raw_dtype, const void* E,
-                   const void* dE, int e_dtype, void* dg, void* dv, int64_t drs, int draw_dtype,
-                   int64_t nb, int64_t T, int64_t hd, float gmin, float gmax, int round_ab,
-                   int compass, const void* e0, void* de0, void* ws, size_t ws_bytes,
-                   cudaStream_t s);
-int lightning_step(const void* qgv, int64_t qrs, int qdt, const void* state, void* new_state,
-                   int sdt, void* z, int zdt, int64_t nb, int64_t C, float gmin, float gmax,
-                   float eps, cudaStream_t s);
 
 inline int dtype_size(int dtype) {
     switch (dtype) {
@@ -46,5 +29,70 @@ inline int dtype_size(int dtype) {
         default: return 0;
     }
 }
+
+enum class Kind { FwdPlain, FwdGated, RevPlain, RevGated };
+
+// A row-strided view: element (row, c) at p + (row * rs + c) * elem_size,
+// row = b * T + t.
+struct View {
+    const char* p;
+    int64_t rs;
+};
+struct MutView {
+    char* p;
+    int64_t rs;
+};
+
+// Arguments common to every scan kernel (trivially copyable).
+struct KArgs {
+    View in[4];
+    MutView out[2];
+    int64_t nb, T, hd;
+    const void* e0;    // acc [nb*hd] or null
+    void* e_last;      // fwd: E_{T-1}; rev: gradient w.r.t. e0 (acc [nb*hd]) or null
+    double gmin, span; // gate_min and gate_max - gate_min
+    int round_ab;
+    unsigned* status;  // device status word
+};
+
+// One scan call after argument checks: kind, element types, arguments.
+struct ScanCall {
+    Kind kind;
+    int tin, te;  // dtype codes of staged logits / A (tin) and of E (te)
+    KArgs a;
+    int compass;
+    void* ws;
+    size_t ws_bytes;
+    cudaStream_t stream;
+    bool bulk_ok;  // every row 16-byte aligned (TMA-stageable)
+};
+
+// Channel-strip scan (no inter-CTA waits).  Sets *taken = false when the
+// problem has too few channels to fill the GPU with strips.
+int strip_scan_launch(const ScanCall& c, bool* taken);
+// Time-chunked scan with decoupled lookback (any shape with aligned rows).
+int lookback_scan_launch(const ScanCall& c);
+// Sequential per-channel scan (any shape, any alignment).
+int sequential_scan_launch(const ScanCall& c);
+size_t lookback_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int compass);
+
+int scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd, int dtype,
+             int compass, const void* e0, void* e_last, void* ws, size_t ws_bytes, cudaStream_t s);
+int scan_rev(const void* A, const void* E, const void* dE, void* dA, void* dB, int64_t nb, int64_t T,
+             int64_t hd, int dtype, int compass, const void* e0, void* de0, void* ws, size_t ws_bytes,
+             cudaStream_t s);
+int gated_scan_fwd(const void* g, const void* v, int64_t rrs, int raw_dtype, void* E, int e_dtype,
+                   int64_t nb, int64_t T, int64_t hd, double gmin, double gmax, int round_ab,
+                   int compass, const void* e0, void* e_last, void* ws, size_t ws_bytes,
+                   cudaStream_t s);
+int gated_scan_bwd(const void* g, const void* v, int64_t rrs, int raw_dtype, const void* E,
+                   const void* dE, int e_dtype, void* dg, void* dv, int64_t drs, int draw_dtype,
+                   int64_t nb, int64_t T, int64_t hd, double gmin, double gmax, int round_ab,
+                   int compass, const void* e0, void* de0, void* ws, size_t ws_bytes,
+                   cudaStream_t s);
+size_t scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int compass);
+int lightning_step(const void* qgv, int64_t qrs, int qdt, const void* state, void* new_state,
+                   int sdt, void* z, int zdt, int64_t nb, int64_t C, double gmin, double gmax,
+                   double eps, cudaStream_t s);
 
 }  // namespace esa

@@ -20,7 +20,7 @@ template <typename Tq, typename Ts, typename Tz>
 __global__ void __launch_bounds__(256) lightning_step_kernel(const Tq* __restrict__ qgv, int64_t qrs,
                                                              const Ts* state, Ts* new_state,
                                                              Tz* __restrict__ z, int64_t C,
-                                                             float gmin, float gmax, float eps) {
+                                                             double gmin, double gspan, double eps) {
     using acc = typename std::conditional<(sizeof(Ts) == 8 || sizeof(Tq) == 8), double, float>::type;
     __shared__ acc red[32];
     const int64_t b = blockIdx.x;
@@ -30,7 +30,7 @@ __global__ void __launch_bounds__(256) lightning_step_kernel(const Tq* __restric
     const Ts* s_in = state + b * C;
     Ts* s_out = new_state + b * C;
     Tz* zr = z + b * C;
-    const acc lo = gmin, span = acc(gmax) - acc(gmin);
+    const acc lo = acc(gmin), span = acc(gspan);
 
     acc ss = acc(0);
     for (int64_t c = threadIdx.x; c < C; c += blockDim.x) {
@@ -79,8 +79,8 @@ static int dispatch_t(int dtype, F&& f) {
 }
 
 int lightning_step(const void* qgv, int64_t qrs, int qdt, const void* state, void* new_state,
-                   int sdt, void* z, int zdt, int64_t nb, int64_t C, float gmin, float gmax,
-                   float eps, cudaStream_t s) {
+                   int sdt, void* z, int zdt, int64_t nb, int64_t C, double gmin, double gmax,
+                   double eps, cudaStream_t s) {
     if (nb < 0 || C <= 0) return set_error(ESA_ERR_INVALID_ARGUMENT, "lightning step needs nb >= 0 and C > 0");
     if (qrs < 3 * C) return set_error(ESA_ERR_INVALID_ARGUMENT, "qgv row stride smaller than 3*C");
     if (nb == 0) return ESA_OK;
@@ -96,7 +96,7 @@ int lightning_step(const void* qgv, int64_t qrs, int qdt, const void* state, voi
                 if (C < 256) threads = (int)((C + 31) / 32 * 32);
                 lightning_step_kernel<Tq, Ts, Tz><<<(unsigned)nb, threads, 0, s>>>(
                     static_cast<const Tq*>(qgv), qrs, static_cast<const Ts*>(state),
-                    static_cast<Ts*>(new_state), static_cast<Tz*>(z), C, gmin, gmax, eps);
+                    static_cast<Ts*>(new_state), static_cast<Tz*>(z), C, gmin, gmax - gmin, eps);
                 cudaError_t e = cudaGetLastError();
                 if (e != cudaSuccess)
                     return set_error(ESA_ERR_CUDA, std::string("lightning launch: ") + cudaGetErrorString(e));

@@ -1,0 +1,350 @@
+// esa_scan_api.cu -- host side of the scans: argument checks, path choice,
+// tensor maps, and the sequential fallback kernel.
+//
+// Path choice for every scan kind:
+//   1. strip scan (esa_strip.cuh) when every row is 16-byte aligned and there
+//      are enough channels to fill the GPU with channel strips;
+//   2. otherwise the time-parallel lookback scan (esa_scan_lookback.cu);
+//   3. rows that are not 16-byte aligned (odd channel counts, offset views):
+//      one thread per channel, sequential over time.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <string>
+
+#include "esa_scan_common.cuh"
+
+namespace esa {
+
+int strip_fwd_plain(const ScanCall& c, bool* taken);
+int strip_rev_plain(const ScanCall& c, bool* taken);
+int strip_fwd_gated(const ScanCall& c, bool* taken);
+int strip_rev_gated(const ScanCall& c, bool* taken);
+
+int strip_scan_launch(const ScanCall& c, bool* taken) {
+    switch (c.kind) {
+        case Kind::FwdPlain: return strip_fwd_plain(c, taken);
+        case Kind::RevPlain: return strip_rev_plain(c, taken);
+        case Kind::FwdGated: return strip_fwd_gated(c, taken);
+        case Kind::RevGated: return strip_rev_gated(c, taken);
+    }
+    *taken = false;
+    return ESA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor maps (driver entry point fetched through the runtime: no -lcuda).
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool encode_strip_map(CUtensorMap* map, int dtype, const void* base, int64_t nb, int64_t T,
+                      int64_t hd, int64_t rs, int ws, int lt, std::string* err) {
+    auto fn = encode_fn();
+    if (!fn) {
+        *err = "cuTensorMapEncodeTiled unavailable";
+        return false;
+    }
+    CUtensorMapDataType dt;
+    switch (dtype) {
+        case ESA_DTYPE_F16: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; break;
+        case ESA_DTYPE_BF16: dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; break;
+        case ESA_DTYPE_F32: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; break;
+        case ESA_DTYPE_F64: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT64; break;
+        default: *err = "dtype"; return false;
+    }
+    const int es = dtype_size(dtype);
+    const cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)T, (cuuint64_t)nb};
+    const cuuint64_t strides[2] = {(cuuint64_t)(rs * es), (cuuint64_t)(T * rs * es)};
+    const cuuint32_t box[3] = {(cuuint32_t)ws, (cuuint32_t)lt, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        *err = "cuTensorMapEncodeTiled error " + std::to_string((int)r);
+        return false;
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// Sequential fallback: one thread per channel, sequential over T.
+// ---------------------------------------------------------------------------
+namespace {
+
+template <Kind K, typename Tin, typename Te>
+__global__ void sequential_scan_kernel(const KArgs prm) {
+    using P = Policy<K, Tin, Te>;
+    using acc = typename P::acc;
+    const int64_t ch = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (ch >= prm.nb * prm.hd) return;
+    const int64_t b = ch / prm.hd, c = ch - b * prm.hd;
+    const acc lo = acc(prm.gmin), span = acc(prm.span);
+    auto ld = [&](int a, int64_t t, auto tag) -> acc {
+        using T = decltype(tag);
+        const T* p = reinterpret_cast<const T*>(prm.in[a].p) + (b * prm.T + t) * prm.in[a].rs + c;
+        return static_cast<acc>(Elem<T>::to_acc(*p));
+    };
+    auto st = [&](int o, int64_t t, acc val, auto tag) {
+        using T = decltype(tag);
+        T* p = reinterpret_cast<T*>(prm.out[o].p) + (b * prm.T + t) * prm.out[o].rs + c;
+        *p = Elem<T>::from_acc(static_cast<typename Elem<T>::acc>(val));
+    };
+    const acc e0v = prm.e0 ? static_cast<const acc*>(prm.e0)[ch] : acc(0);
+    if constexpr (!P::REV) {
+        acc e = e0v;
+        for (int64_t t = 0; t < prm.T; ++t) {
+            acc a, bb;
+            if constexpr (K == Kind::FwdPlain) {
+                a = ld(0, t, Tin{});
+                bb = ld(1, t, Tin{});
+            } else {
+                a = lo + span * sigmoid_(ld(0, t, Tin{}));
+                bb = (acc(1) - a) * tanh_(ld(1, t, Tin{}));
+                if (prm.round_ab) {
+                    a = round_to<Te>(a);
+                    bb = round_to<Te>(bb);
+                }
+            }
+            e = a * e + bb;
+            st(0, t, e, Te{});
+        }
+        if (prm.e_last) static_cast<acc*>(prm.e_last)[ch] = e;
+    } else {
+        acc h = acc(0);
+        for (int64_t t = prm.T - 1; t >= 0; --t) {
+            if constexpr (K == Kind::RevPlain) {
+                const acc a = ld(0, t, Te{});
+                const acc d = ld(2, t, Te{});
+                const acc ep = t > 0 ? ld(1, t - 1, Te{}) : e0v;
+                const acc g = d + h;
+                st(0, t, g * ep, Te{});
+                st(1, t, g, Te{});
+                h = a * g;
+            } else {
+                const acc sg = sigmoid_(ld(0, t, Tin{}));
+                const acc A = lo + span * sg;
+                const acc Ar = prm.round_ab ? round_to<Te>(A) : A;
+                const acc V = tanh_(ld(1, t, Tin{}));
+                const acc d = ld(3, t, Te{});
+                const acc ep = t > 0 ? ld(2, t - 1, Te{}) : e0v;
+                const acc g = d + h;
+                st(0, t, (g * ep - g * V) * span * sg * (acc(1) - sg), Tin{});
+                st(1, t, g * (acc(1) - A) * (acc(1) - V * V), Tin{});
+                h = Ar * g;
+            }
+        }
+        if (prm.e_last) static_cast<acc*>(prm.e_last)[ch] = h;
+    }
+}
+
+template <Kind K, typename Tin, typename Te>
+int seq_typed(const ScanCall& c) {
+    const int threads = 256;
+    const int64_t nch = c.a.nb * c.a.hd;
+    const int64_t blocks = (nch + threads - 1) / threads;
+    sequential_scan_kernel<K, Tin, Te><<<(unsigned)blocks, threads, 0, c.stream>>>(c.a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("sequential scan launch: ") + cudaGetErrorString(e));
+    return ESA_OK;
+}
+
+}  // namespace
+
+int sequential_scan_launch(const ScanCall& c) {
+    return dispatch_dtype(c.tin, [&](auto ti) -> int {
+        using Tin = decltype(ti);
+        return dispatch_dtype(c.te, [&](auto tee) -> int {
+            using Te = decltype(tee);
+            switch (c.kind) {
+                case Kind::FwdPlain:
+                    if constexpr (std::is_same<Tin, Te>::value) return seq_typed<Kind::FwdPlain, Tin, Te>(c);
+                    break;
+                case Kind::RevPlain:
+                    if constexpr (std::is_same<Tin, Te>::value) return seq_typed<Kind::RevPlain, Tin, Te>(c);
+                    break;
+                case Kind::FwdGated: return seq_typed<Kind::FwdGated, Tin, Te>(c);
+                case Kind::RevGated: return seq_typed<Kind::RevGated, Tin, Te>(c);
+            }
+            return set_error(ESA_ERR_UNSUPPORTED_DTYPE, "plain scans need one dtype");
+        });
+    });
+}
+
+// ---------------------------------------------------------------------------
+// Entry points behind the C ABI.
+// ---------------------------------------------------------------------------
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool rows_aligned(const void* p, int64_t rs, int64_t hd, int es) {
+    return aligned16(p) && ((rs * es) % 16 == 0) && ((hd * es) % 16 == 0);
+}
+
+int check_dims(int64_t nb, int64_t T, int64_t hd, int compass) {
+    if (nb < 0 || T < 0 || hd < 0) return set_error(ESA_ERR_INVALID_ARGUMENT, "negative dimension");
+    if (compass <= 0) return set_error(ESA_ERR_INVALID_ARGUMENT, "compass must be a positive integer");
+    if (T > 0x7fffffffLL || nb > 0x7fffffffLL || hd > 0x7fffffffLL)
+        return set_error(ESA_ERR_INVALID_ARGUMENT, "dimension exceeds 2^31 - 1");
+    return ESA_OK;
+}
+
+int run(ScanCall& c) {
+    if (c.a.nb == 0 || c.a.T == 0 || c.a.hd == 0) return ESA_OK;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    c.a.status = status_ptr(dev);
+    if (c.a.status == nullptr) return set_error(ESA_ERR_CUDA, "cannot resolve the device status word");
+    if (!c.bulk_ok) return sequential_scan_launch(c);
+    bool taken = false;
+    const int rc = strip_scan_launch(c, &taken);
+    if (rc != ESA_OK || taken) return rc;
+    return lookback_scan_launch(c);
+}
+
+}  // namespace
+
+size_t scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int compass) {
+    return lookback_workspace_bytes(nb, T, hd, wide_es, compass);
+}
+
+int scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd, int dtype,
+             int compass, const void* e0, void* e_last, void* ws, size_t ws_bytes, cudaStream_t s) {
+    if (int rc = check_dims(nb, T, hd, compass)) return rc;
+    const int es = dtype_size(dtype);
+    if (es == 0) return set_error(ESA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code " + std::to_string(dtype));
+    if (nb * T * hd > 0 && (!A || !B || !E)) return set_error(ESA_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    ScanCall c{};
+    c.kind = Kind::FwdPlain;
+    c.tin = c.te = dtype;
+    c.a.in[0] = {static_cast<const char*>(A), hd};
+    c.a.in[1] = {static_cast<const char*>(B), hd};
+    c.a.out[0] = {static_cast<char*>(E), hd};
+    c.a.nb = nb;
+    c.a.T = T;
+    c.a.hd = hd;
+    c.a.e0 = e0;
+    c.a.e_last = e_last;
+    c.compass = compass;
+    c.ws = ws;
+    c.ws_bytes = ws_bytes;
+    c.stream = s;
+    c.bulk_ok = rows_aligned(A, hd, hd, es) && rows_aligned(B, hd, hd, es) && rows_aligned(E, hd, hd, es);
+    return run(c);
+}
+
+int scan_rev(const void* A, const void* E, const void* dE, void* dA, void* dB, int64_t nb, int64_t T,
+             int64_t hd, int dtype, int compass, const void* e0, void* de0, void* ws, size_t ws_bytes,
+             cudaStream_t s) {
+    if (int rc = check_dims(nb, T, hd, compass)) return rc;
+    const int es = dtype_size(dtype);
+    if (es == 0) return set_error(ESA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code " + std::to_string(dtype));
+    if (nb * T * hd > 0 && (!A || !E || !dE || !dA || !dB))
+        return set_error(ESA_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    ScanCall c{};
+    c.kind = Kind::RevPlain;
+    c.tin = c.te = dtype;
+    c.a.in[0] = {static_cast<const char*>(A), hd};
+    c.a.in[1] = {static_cast<const char*>(E), hd};
+    c.a.in[2] = {static_cast<const char*>(dE), hd};
+    c.a.out[0] = {static_cast<char*>(dA), hd};
+    c.a.out[1] = {static_cast<char*>(dB), hd};
+    c.a.nb = nb;
+    c.a.T = T;
+    c.a.hd = hd;
+    c.a.e0 = e0;
+    c.a.e_last = de0;
+    c.compass = compass;
+    c.ws = ws;
+    c.ws_bytes = ws_bytes;
+    c.stream = s;
+    c.bulk_ok = rows_aligned(A, hd, hd, es) && rows_aligned(E, hd, hd, es) && rows_aligned(dE, hd, hd, es) &&
+                rows_aligned(dA, hd, hd, es) && rows_aligned(dB, hd, hd, es);
+    return run(c);
+}
+
+int gated_scan_fwd(const void* g, const void* v, int64_t rrs, int raw_dtype, void* E, int e_dtype,
+                   int64_t nb, int64_t T, int64_t hd, double gmin, double gmax, int round_ab,
+                   int compass, const void* e0, void* e_last, void* ws, size_t ws_bytes,
+                   cudaStream_t s) {
+    if (int rc = check_dims(nb, T, hd, compass)) return rc;
+    const int ei = dtype_size(raw_dtype), ee = dtype_size(e_dtype);
+    if (ei == 0 || ee == 0) return set_error(ESA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code");
+    if (nb * T * hd > 0 && (!g || !v || !E)) return set_error(ESA_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (rrs < hd) return set_error(ESA_ERR_INVALID_ARGUMENT, "raw_row_stride smaller than hd");
+    ScanCall c{};
+    c.kind = Kind::FwdGated;
+    c.tin = raw_dtype;
+    c.te = e_dtype;
+    c.a.in[0] = {static_cast<const char*>(g), rrs};
+    c.a.in[1] = {static_cast<const char*>(v), rrs};
+    c.a.out[0] = {static_cast<char*>(E), hd};
+    c.a.nb = nb;
+    c.a.T = T;
+    c.a.hd = hd;
+    c.a.e0 = e0;
+    c.a.e_last = e_last;
+    c.a.gmin = gmin;
+    c.a.span = gmax - gmin;
+    c.a.round_ab = round_ab;
+    c.compass = compass;
+    c.ws = ws;
+    c.ws_bytes = ws_bytes;
+    c.stream = s;
+    c.bulk_ok = rows_aligned(g, rrs, hd, ei) && rows_aligned(v, rrs, hd, ei) && rows_aligned(E, hd, hd, ee);
+    return run(c);
+}
+
+int gated_scan_bwd(const void* g, const void* v, int64_t rrs, int raw_dtype, const void* E,
+                   const void* dE, int e_dtype, void* dg, void* dv, int64_t drs, int draw_dtype,
+                   int64_t nb, int64_t T, int64_t hd, double gmin, double gmax, int round_ab,
+                   int compass, const void* e0, void* de0, void* ws, size_t ws_bytes,
+                   cudaStream_t s) {
+    if (int rc = check_dims(nb, T, hd, compass)) return rc;
+    const int ei = dtype_size(raw_dtype), ee = dtype_size(e_dtype);
+    if (ei == 0 || ee == 0) return set_error(ESA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code");
+    if (nb * T * hd > 0 && (!g || !v || !E || !dE || !dg || !dv))
+        return set_error(ESA_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (rrs < hd || drs < hd) return set_error(ESA_ERR_INVALID_ARGUMENT, "row stride smaller than hd");
+    if (draw_dtype != raw_dtype)
+        return set_error(ESA_ERR_UNSUPPORTED_DTYPE, "d_gate_raw/d_value_raw must have the dtype of gate_raw/value_raw");
+    ScanCall c{};
+    c.kind = Kind::RevGated;
+    c.tin = raw_dtype;
+    c.te = e_dtype;
+    c.a.in[0] = {static_cast<const char*>(g), rrs};
+    c.a.in[1] = {static_cast<const char*>(v), rrs};
+    c.a.in[2] = {static_cast<const char*>(E), hd};
+    c.a.in[3] = {static_cast<const char*>(dE), hd};
+    c.a.out[0] = {static_cast<char*>(dg), drs};
+    c.a.out[1] = {static_cast<char*>(dv), drs};
+    c.a.nb = nb;
+    c.a.T = T;
+    c.a.hd = hd;
+    c.a.e0 = e0;
+    c.a.e_last = de0;
+    c.a.gmin = gmin;
+    c.a.span = gmax - gmin;
+    c.a.round_ab = round_ab;
+    c.compass = compass;
+    c.ws = ws;
+    c.ws_bytes = ws_bytes;
+    c.stream = s;
+    c.bulk_ok = rows_aligned(g, rrs, hd, ei) && rows_aligned(v, rrs, hd, ei) && rows_aligned(E, hd, hd, ee) &&
+                rows_aligned(dE, hd, hd, ee) && rows_aligned(dg, drs, hd, ei) && rows_aligned(dv, drs, hd, ei);
+    return run(c);
+}
+
+}  // namespace esa

@@ -1,0 +1,238 @@
+// esa_scan_common.cuh -- definitions shared by the scan kernels.
+//
+// The recurrence E_t = A_t E_{t-1} + B_t runs over independent channels
+// (b, c), c < hd, of [nb, T, hd] data (hd contiguous, the reference's
+// [B,T,H,D]).  Four kinds of scan share one per-step contract:
+//
+//   FwdPlain  staged {A, B}                 -> E
+//   FwdGated  staged {g, v} (logits)         -> E, with A = gmin + span*sigmoid(g),
+//                                               B = (1 - A) tanh(v) computed in-kernel
+//   RevPlain  staged {A, E_{t-1}, dE}        -> dA, dB
+//   RevGated  staged {g, v, E_{t-1}, dE}     -> d g, d v  (gate chain rule fused)
+//
+// Every kind is an affine scan x_t = a_t x_{t-1} + b_t (forward in t) or
+// x_t = a_t x_{t+1} + b_t (reverse, with x = H = A*G, a = A_t, b = A_t dE_t).
+// Phase 1 of a kernel produces (a_t, b_t) per step ("step_coef"); phase 3
+// re-runs the steps from the exact incoming state and writes the outputs
+// ("step_apply").
+#pragma once
+
+#include <type_traits>
+
+#include <string>
+
+#include "esa_common.cuh"
+#include "esa_internal.h"
+
+namespace esa {
+
+// Calls f(T{}) with T the element type of dtype code `dtype`.
+template <typename F>
+int dispatch_dtype(int dtype, F&& f) {
+    switch (dtype) {
+        case ESA_DTYPE_F16: return f(__half{});
+        case ESA_DTYPE_BF16: return f(__nv_bfloat16{});
+        case ESA_DTYPE_F32: return f(float{});
+        case ESA_DTYPE_F64: return f(double{});
+        default: return set_error(ESA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code " + std::to_string(dtype));
+    }
+}
+
+template <typename T, int N>
+struct alignas(sizeof(T) * N) VecN {
+    T v[N];
+};
+
+template <typename T>
+__device__ __forceinline__ float round_to(float x) {
+    return Elem<T>::to_acc(Elem<T>::from_acc(x));
+}
+template <typename T>
+__device__ __forceinline__ double round_to(double x) {
+    return static_cast<double>(Elem<T>::from_acc(static_cast<typename Elem<T>::acc>(x)));
+}
+
+template <Kind K, typename Tin, typename Te>
+struct Policy {
+    static constexpr bool REV = (K == Kind::RevPlain || K == Kind::RevGated);
+    static constexpr bool GATED = (K == Kind::FwdGated || K == Kind::RevGated);
+    static constexpr int NIN = (K == Kind::RevGated) ? 4 : (K == Kind::RevPlain ? 3 : 2);
+    using acc = typename std::conditional<(sizeof(Tin) == 8 || sizeof(Te) == 8), double, float>::type;
+    static constexpr int WIDE = (sizeof(Tin) > sizeof(Te)) ? sizeof(Tin) : sizeof(Te);
+    static constexpr int VEC = 16 / WIDE;  // channels per thread vector
+    // element size of staged array i
+    static __host__ __device__ constexpr int es(int i) {
+        return (K == Kind::RevGated) ? (i < 2 ? (int)sizeof(Tin) : (int)sizeof(Te))
+               : (K == Kind::RevPlain) ? (int)sizeof(Te)
+                                       : (int)sizeof(Tin);
+    }
+    // staged array i holds row t + shift(i) at step t (E_{t-1} for the reverse scans)
+    static __host__ __device__ constexpr int shift(int i) {
+        return (K == Kind::RevPlain && i == 1) || (K == Kind::RevGated && i == 2) ? -1 : 0;
+    }
+    // phase-1 values kept in registers for phase 3 (S rows x VEC channels)
+    template <int S>
+    struct Cache {
+        acc c0[S][GATED ? VEC : 1];
+        acc c1[S][(K == Kind::FwdGated) ? VEC : 1];
+    };
+};
+
+template <typename T, int N, typename A>
+__device__ __forceinline__ void load_smem(const char* p, A (&out)[N]) {
+    VecN<T, N> v = *reinterpret_cast<const VecN<T, N>*>(p);
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = static_cast<A>(Elem<T>::to_acc(v.v[i]));
+}
+
+template <typename T, int N, typename A>
+__device__ __forceinline__ void store_global(char* p, const A (&in)[N]) {
+    VecN<T, N> v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) v.v[i] = Elem<T>::from_acc(static_cast<typename Elem<T>::acc>(in[i]));
+    *reinterpret_cast<VecN<T, N>*>(p) = v;
+}
+
+// Per-step coefficients (a, b) of step row `rows` (phase 1).  `rows[i]` points
+// at this thread's first channel in staged array i.
+template <Kind K, typename Tin, typename Te, int S, typename P = Policy<K, Tin, Te>>
+__device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KArgs& prm,
+                                          typename P::acc (&a)[P::VEC],
+                                          typename P::acc (&b)[P::VEC],
+                                          typename P::template Cache<S>& cache, int s) {
+    using acc = typename P::acc;
+    constexpr int VEC = P::VEC;
+    if constexpr (K == Kind::FwdPlain) {
+        load_smem<Tin, VEC>(rows[0], a);
+        load_smem<Tin, VEC>(rows[1], b);
+    } else if constexpr (K == Kind::FwdGated) {
+        acc g[VEC], v[VEC];
+        load_smem<Tin, VEC>(rows[0], g);
+        load_smem<Tin, VEC>(rows[1], v);
+        const acc lo = acc(prm.gmin), span = acc(prm.span);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+            acc A = lo + span * sigmoid_(g[i]);
+            acc B = (acc(1) - A) * tanh_(v[i]);
+            if (prm.round_ab) {
+                A = round_to<Te>(A);
+                B = round_to<Te>(B);
+            }
+            a[i] = A;
+            b[i] = B;
+            cache.c0[s][i] = A;
+            cache.c1[s][i] = B;
+        }
+    } else if constexpr (K == Kind::RevPlain) {
+        acc d[VEC];
+        load_smem<Te, VEC>(rows[0], a);
+        load_smem<Te, VEC>(rows[2], d);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) b[i] = a[i] * d[i];
+    } else {  // RevGated
+        acc g[VEC], d[VEC];
+        load_smem<Tin, VEC>(rows[0], g);
+        load_smem<Te, VEC>(rows[3], d);
+        const acc lo = acc(prm.gmin), span = acc(prm.span);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+            const acc sg = sigmoid_(g[i]);
+            acc A = lo + span * sg;
+            if (prm.round_ab) A = round_to<Te>(A);
+            cache.c0[s][i] = sg;
+            a[i] = A;
+            b[i] = A * d[i];
+        }
+    }
+}
+
+// Phase-3 step: advance the state `e` over step t and write this step's
+// outputs for VEC channels starting at global channel `gc` (when `valid`).
+// Forward: e = E_{t-1} in, E_t out.  Reverse: e = H_{t+1} in, H_t out.
+template <Kind K, typename Tin, typename Te, int S, typename P = Policy<K, Tin, Te>>
+__device__ __forceinline__ void step_apply(const char* const (&rows)[4], const KArgs& prm,
+                                           int64_t b, int64_t t, int64_t gc, bool valid,
+                                           typename P::acc (&e)[P::VEC],
+                                           typename P::template Cache<S>& cache, int s) {
+    using acc = typename P::acc;
+    constexpr int VEC = P::VEC;
+    const int64_t orow = b * prm.T + t;
+    if constexpr (K == Kind::FwdPlain) {
+        acc a[VEC], bb[VEC];
+        load_smem<Tin, VEC>(rows[0], a);
+        load_smem<Tin, VEC>(rows[1], bb);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) e[i] = a[i] * e[i] + bb[i];
+        if (valid)
+            store_global<Te, VEC>(prm.out[0].p + (orow * prm.out[0].rs + gc) * (int64_t)sizeof(Te), e);
+    } else if constexpr (K == Kind::FwdGated) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) e[i] = cache.c0[s][i] * e[i] + cache.c1[s][i];
+        if (valid)
+            store_global<Te, VEC>(prm.out[0].p + (orow * prm.out[0].rs + gc) * (int64_t)sizeof(Te), e);
+    } else {
+        acc ep[VEC], d[VEC];
+        load_smem<Te, VEC>(K == Kind::RevPlain ? rows[2] : rows[3], d);
+        if (t > 0) {
+            load_smem<Te, VEC>(K == Kind::RevPlain ? rows[1] : rows[2], ep);
+        } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) ep[i] = acc(0);
+            if (prm.e0 != nullptr && valid) {
+                const acc* e0 = static_cast<const acc*>(prm.e0) + b * prm.hd + gc;
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) ep[i] = e0[i];
+            }
+        }
+        if constexpr (K == Kind::RevPlain) {
+            acc a[VEC], ga[VEC];
+            load_smem<Te, VEC>(rows[0], a);
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                const acc g = d[i] + e[i];
+                ga[i] = g * ep[i];
+                d[i] = g;  // dB
+                e[i] = a[i] * g;
+            }
+            if (valid) {
+                store_global<Te, VEC>(prm.out[0].p + (orow * prm.out[0].rs + gc) * (int64_t)sizeof(Te), ga);
+                store_global<Te, VEC>(prm.out[1].p + (orow * prm.out[1].rs + gc) * (int64_t)sizeof(Te), d);
+            }
+        } else {
+            acc v[VEC], dg[VEC], dv[VEC];
+            load_smem<Tin, VEC>(rows[1], v);
+            const acc lo = acc(prm.gmin), span = acc(prm.span);
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                const acc sg = cache.c0[s][i];
+                const acc A = lo + span * sg;
+                const acc Ar = prm.round_ab ? round_to<Te>(A) : A;
+                const acc V = tanh_(v[i]);
+                const acc g = d[i] + e[i];
+                const acc dA = g * ep[i];
+                dg[i] = (dA - g * V) * span * sg * (acc(1) - sg);
+                dv[i] = g * (acc(1) - A) * (acc(1) - V * V);
+                e[i] = Ar * g;
+            }
+            if (valid) {
+                store_global<Tin, VEC>(prm.out[0].p + (orow * prm.out[0].rs + gc) * (int64_t)sizeof(Tin), dg);
+                store_global<Tin, VEC>(prm.out[1].p + (orow * prm.out[1].rs + gc) * (int64_t)sizeof(Tin), dv);
+            }
+        }
+    }
+}
+
+// Bounded wait on an mbarrier phase.  Returns false (and raises `status`) if
+// the phase did not complete within the wait budget.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity, unsigned* status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    for (unsigned it = 0; it < kWaitMaxIters; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitBudgetNs) break;
+    }
+    atomicOr(status, ESA_STATUS_COPY_TIMEOUT);
+    return false;
+}
+
+}  // namespace esa

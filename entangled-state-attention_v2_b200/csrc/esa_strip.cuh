@@ -1,0 +1,464 @@
+// esa_strip.cuh -- channel-strip scan: the main path of every scan kind.
+//
+// A CTA owns a strip of WS = LPR*VEC consecutive channels of one batch row and
+// sweeps the whole time axis through it, tile by tile (LT steps per tile).
+// The recurrence state never leaves the chip between tiles, so there is no
+// inter-CTA communication and no waiting on other CTAs at all; the only waits
+// are on this CTA's own TMA copies.  Parallelism comes from the channel
+// count: nb*hd channels give nb*ceil(hd/WS) strips (e.g. 512 for the
+// [32, 4096, 16, 64] fp16 microbenchmark with 64-channel strips).
+//
+// Data movement.  One thread issues 3-D tiled TMA loads
+// (cp.async.bulk.tensor.3d, tensor map [nb, T, hd], box [1, LT, WS], L2
+// evict-first) of every staged array into an NSTAGE-deep ring of shared-memory
+// stages, completing on one mbarrier per stage; the CTA consumes stage j while
+// the next NSTAGE-1 tiles are in flight.  Outputs are stored from registers
+// with 16-byte coalesced stores.  Each input byte crosses HBM once, each
+// output byte once: the kernel's DRAM traffic is exactly the algorithmic one.
+//
+// Work inside a tile (8 warps).  Lane l of warp w owns channel vector
+// cl = l % LPR (VEC channels, one 16-byte vector of the widest type) of row
+// group rg = w*(32/LPR) + l/LPR, i.e. SR consecutive steps:
+//   phase 1: compose the row group's SR steps into an affine pair (a, b);
+//   warp:    inclusive Kogge-Stone scan of the pairs across the warp's row
+//            groups with warp shuffles (lanes LPR apart share channels);
+//   CTA:     warp totals through shared memory -> exclusive prefix per warp;
+//   phase 3: re-run the SR steps from the exact incoming state
+//            (carry o warp prefix o row-group prefix) and write the outputs;
+//            the last row group leaves the tile's final state as the carry of
+//            the next tile.
+// Reverse kinds run the tiles and steps in descending time.
+#pragma once
+
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <string>
+
+#include "esa_scan_common.cuh"
+
+namespace esa {
+
+struct StripParams {
+    KArgs a;
+    int64_t spr;     // strips per batch row = ceil(hd / WS)
+    int64_t nitems;  // nb * spr
+    int64_t ntt;     // tiles along T = ceil(T / LT)
+    int nstage;
+};
+
+template <Kind K, typename Tin, typename Te, int LPR_, int SR_>
+struct StripCfg {
+    using P = Policy<K, Tin, Te>;
+    static constexpr int LPR = LPR_;
+    static constexpr int SR = SR_;
+    static constexpr int NW = 8;
+    static constexpr int NT = 32 * NW;
+    static constexpr int VEC = P::VEC;
+    static constexpr int RGW = 32 / LPR;  // row groups per warp
+    static constexpr int RG = NW * RGW;   // row groups per CTA
+    static constexpr int LT = RG * SR;    // steps per tile
+    static constexpr int WS = LPR * VEC;  // channels per strip
+    static __host__ __device__ constexpr int row_bytes(int a) { return WS * P::es(a); }
+    static __host__ __device__ constexpr int array_off(int a) {
+        int o = 0;
+        for (int i = 0; i < a; ++i) o += LT * row_bytes(i);
+        return o;
+    }
+    static __host__ __device__ constexpr int stage_bytes() { return array_off(P::NIN); }
+    static size_t smem_bytes(int nstage) {
+        return (size_t)nstage * stage_bytes() + (2 * NW * WS + 2 * WS) * sizeof(typename P::acc) +
+               (size_t)nstage * sizeof(uint64_t) + 128;
+    }
+};
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int x, int y,
+                                            int z, uint64_t* bar, uint64_t policy) {
+    const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    const uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;"
+        :: "r"(d), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(b), "l"(policy)
+        : "memory");
+}
+
+template <class Cfg>
+__device__ __forceinline__ void strip_issue(const StripParams& prm, const CUtensorMap* const (&maps)[4],
+                                            char* stage, uint64_t* bar, int64_t b, int64_t strip,
+                                            int64_t t0, uint64_t policy) {
+    using P = typename Cfg::P;
+    mbar_arrive_expect_tx(bar, (unsigned)Cfg::stage_bytes());
+#pragma unroll
+    for (int a = 0; a < P::NIN; ++a)
+        tma_load_3d(stage + Cfg::array_off(a), maps[a], (int)(strip * Cfg::WS),
+                    (int)(t0 + P::shift(a)), (int)b, bar, policy);
+}
+
+template <Kind K, typename Tin, typename Te, int LPR, int SR>
+__global__ void __launch_bounds__(256) strip_scan_kernel(const StripParams prm,
+                                                         const __grid_constant__ CUtensorMap m0,
+                                                         const __grid_constant__ CUtensorMap m1,
+                                                         const __grid_constant__ CUtensorMap m2,
+                                                         const __grid_constant__ CUtensorMap m3) {
+    using Cfg = StripCfg<K, Tin, Te, LPR, SR>;
+    using P = typename Cfg::P;
+    using acc = typename P::acc;
+    constexpr int VEC = P::VEC;
+    constexpr int WS = Cfg::WS;
+    constexpr int NW = Cfg::NW;
+    constexpr int RGW = Cfg::RGW;
+    constexpr int LT = Cfg::LT;
+    constexpr unsigned FULL = 0xffffffffu;
+    const KArgs& ka = prm.a;
+    const int nstage = prm.nstage;
+
+    extern __shared__ __align__(128) char smem_raw[];
+    char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    acc* wagg_a = reinterpret_cast<acc*>(smem + (size_t)nstage * Cfg::stage_bytes());
+    acc* wagg_b = wagg_a + NW * WS;
+    acc* carry = wagg_b + NW * WS;  // [2][WS], double-buffered by tile parity
+    uint64_t* bars = reinterpret_cast<uint64_t*>(carry + 2 * WS);
+
+    const CUtensorMap* maps[4] = {&m0, &m1, &m2, &m3};
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int rgl = lane / LPR;         // row group within the warp
+    const int cl = lane - rgl * LPR;    // channel vector within the strip
+    const int rg = warp * RGW + rgl;    // row group within the tile
+    const int c = cl * VEC;             // first channel of this thread within the strip
+    // the row group that processes a tile's last steps (carries the state on)
+    const bool last_rg = P::REV ? (rg == 0) : (rg == Cfg::RG - 1);
+    const bool last_rgl = P::REV ? (rgl == 0) : (rgl == RGW - 1);
+
+    const uint64_t policy = policy_evict_first();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < nstage; ++s) mbar_init(&bars[s], 1);
+        fence_mbarrier_init();
+    }
+    __syncthreads();
+
+    uint64_t used = 0;    // tiles consumed by this CTA so far (stage = used % nstage)
+    uint64_t issued = 0;  // tiles whose copies this CTA has issued
+    bool aborted = false;
+    for (int64_t item = blockIdx.x; item < prm.nitems && !aborted; item += gridDim.x) {
+        const int64_t b = item / prm.spr;
+        const int64_t strip = item - b * prm.spr;
+        const int64_t gc = strip * WS + c;  // first global channel of this thread
+        const bool valid = gc < ka.hd;
+        auto tile_t0 = [&](int64_t j) -> int64_t {
+            return (P::REV ? (prm.ntt - 1 - j) : j) * (int64_t)LT;
+        };
+        // initial carry: e0 (forward) or zero (reverse: nothing after T)
+        if (rgl == 0 && warp == 0) {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                acc x = acc(0);
+                if (!P::REV && ka.e0 != nullptr && valid) x = static_cast<const acc*>(ka.e0)[b * ka.hd + gc + i];
+                carry[c + i] = x;  // slot 0
+            }
+        }
+        // prologue: fill the ring
+        const int npro = (int)(prm.ntt < nstage ? prm.ntt : nstage);
+        if (threadIdx.x == 0) {
+            for (int s = 0; s < npro; ++s) {
+                const int slot = (int)((used + s) % nstage);
+                strip_issue<Cfg>(prm, maps, smem + (size_t)slot * Cfg::stage_bytes(), &bars[slot], b,
+                                 strip, tile_t0(s), policy);
+            }
+        }
+        issued += npro;
+        __syncthreads();
+
+        for (int64_t j = 0; j < prm.ntt; ++j, ++used) {
+            const int slot = (int)(used % nstage);
+            const unsigned parity = (unsigned)((used / nstage) & 1);
+            const int cur = (int)(j & 1);
+            const int64_t t0 = tile_t0(j);
+            const bool ok = mbar_wait_bounded(&bars[slot], parity, ka.status);
+            const char* sbase = smem + (size_t)slot * Cfg::stage_bytes();
+            auto rows_at = [&](int r, const char* (&rows)[4]) {
+#pragma unroll
+                for (int a = 0; a < 4; ++a)
+                    rows[a] = a < P::NIN ? sbase + Cfg::array_off(a) + r * Cfg::row_bytes(a) + c * P::es(a)
+                                         : nullptr;
+            };
+
+            // ---- phase 1: this row group's SR steps ------------------------
+            typename P::template Cache<SR> cache;
+            acc pa[VEC], pb[VEC];
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                pa[i] = acc(1);
+                pb[i] = acc(0);
+            }
+#pragma unroll
+            for (int ss = 0; ss < SR; ++ss) {
+                const int s = P::REV ? (SR - 1 - ss) : ss;
+                const int r = rg * SR + s;
+                if (t0 + r < ka.T) {
+                    const char* rows[4];
+                    rows_at(r, rows);
+                    acc a[VEC], bb[VEC];
+                    step_coef<K, Tin, Te, SR>(rows, ka, a, bb, cache, s);
+#pragma unroll
+                    for (int i = 0; i < VEC; ++i) {
+                        pb[i] = a[i] * pb[i] + bb[i];
+                        pa[i] = a[i] * pa[i];
+                    }
+                }
+            }
+            // ---- warp: inclusive scan over row groups (shuffles) -----------
+#pragma unroll
+            for (int d = 1; d < RGW; d <<= 1) {
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) {
+                    acc qa, qb;
+                    if constexpr (P::REV) {
+                        qa = __shfl_down_sync(FULL, pa[i], d * LPR);
+                        qb = __shfl_down_sync(FULL, pb[i], d * LPR);
+                    } else {
+                        qa = __shfl_up_sync(FULL, pa[i], d * LPR);
+                        qb = __shfl_up_sync(FULL, pb[i], d * LPR);
+                    }
+                    const bool take = P::REV ? (rgl + d < RGW) : (rgl >= d);
+                    if (take) {
+                        pb[i] = pa[i] * qb + pb[i];
+                        pa[i] = pa[i] * qa;
+                    }
+                }
+            }
+            // exclusive prefix of this row group within the warp
+            acc xa[VEC], xb[VEC];
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                acc qa, qb;
+                if constexpr (RGW > 1) {
+                    if constexpr (P::REV) {
+                        qa = __shfl_down_sync(FULL, pa[i], LPR);
+                        qb = __shfl_down_sync(FULL, pb[i], LPR);
+                    } else {
+                        qa = __shfl_up_sync(FULL, pa[i], LPR);
+                        qb = __shfl_up_sync(FULL, pb[i], LPR);
+                    }
+                } else {
+                    qa = acc(1);
+                    qb = acc(0);
+                }
+                const bool first = P::REV ? (rgl == RGW - 1) : (rgl == 0);
+                xa[i] = first ? acc(1) : qa;
+                xb[i] = first ? acc(0) : qb;
+            }
+            if (last_rgl) {
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) {
+                    wagg_a[warp * WS + c + i] = pa[i];
+                    wagg_b[warp * WS + c + i] = pb[i];
+                }
+            }
+            __syncthreads();
+
+            // ---- CTA: exclusive prefix over the warps before this one -------
+            acc ea[VEC], eb[VEC];
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                ea[i] = acc(1);
+                eb[i] = acc(0);
+            }
+#pragma unroll
+            for (int n = 0; n < NW; ++n) {
+                const int w = P::REV ? (NW - 1 - n) : n;
+                if (w == warp) break;
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) {
+                    const acc aw = wagg_a[w * WS + c + i];
+                    const acc bw = wagg_b[w * WS + c + i];
+                    eb[i] = aw * eb[i] + bw;
+                    ea[i] = aw * ea[i];
+                }
+            }
+            // ---- phase 3: incoming state, re-run, outputs ------------------
+            acc e[VEC];
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                const acc x = ea[i] * carry[cur * WS + c + i] + eb[i];
+                e[i] = xa[i] * x + xb[i];
+            }
+#pragma unroll
+            for (int ss = 0; ss < SR; ++ss) {
+                const int s = P::REV ? (SR - 1 - ss) : ss;
+                const int r = rg * SR + s;
+                const int64_t t = t0 + r;
+                if (t < ka.T) {
+                    const char* rows[4];
+                    rows_at(r, rows);
+                    step_apply<K, Tin, Te, SR>(rows, ka, b, t, gc, valid, e, cache, s);
+                }
+            }
+            if (last_rg) {
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) carry[(cur ^ 1) * WS + c + i] = e[i];
+            }
+            // stage `slot` consumed, next carry visible; the whole CTA stops if
+            // any thread's copy wait ran out
+            if (__syncthreads_or(!ok)) {
+                aborted = true;
+                break;
+            }
+            if (j + nstage < prm.ntt) {
+                if (threadIdx.x == 0)
+                    strip_issue<Cfg>(prm, maps, smem + (size_t)slot * Cfg::stage_bytes(), &bars[slot],
+                                     b, strip, tile_t0(j + nstage), policy);
+                ++issued;
+            }
+        }
+        if (aborted) break;
+        // final state: E_{T-1} (forward) or the gradient w.r.t. e0 (reverse)
+        if (ka.e_last != nullptr && rgl == 0 && warp == 0 && valid) {
+            const int fin = (int)(prm.ntt & 1);
+#pragma unroll
+            for (int i = 0; i < VEC; ++i)
+                static_cast<acc*>(ka.e_last)[b * ka.hd + gc + i] = carry[fin * WS + c + i];
+        }
+        __syncthreads();
+    }
+    // after a failed wait, give every copy still in flight one more bounded
+    // wait, so that no TMA copy targets this CTA's shared memory after exit
+    for (uint64_t u = used; u < issued; ++u)
+        mbar_wait_bounded(&bars[u % nstage], (unsigned)((u / nstage) & 1), ka.status);
+}
+
+// Build a 3-D tensor map [nb][T][hd] (row stride rs elements) with box
+// [1][LT][WS] for dtype code `dtype`.
+bool encode_strip_map(CUtensorMap* map, int dtype, const void* base, int64_t nb, int64_t T,
+                      int64_t hd, int64_t rs, int ws, int lt, std::string* err);
+
+template <Kind K, typename Tin, typename Te, int LPR, int SR>
+int strip_launch_typed(const ScanCall& call, int nstage, int grid) {
+    using Cfg = StripCfg<K, Tin, Te, LPR, SR>;
+    using P = typename Cfg::P;
+    StripParams prm{};
+    prm.a = call.a;
+    prm.spr = (call.a.hd + Cfg::WS - 1) / Cfg::WS;
+    prm.nitems = call.a.nb * prm.spr;
+    prm.ntt = (call.a.T + Cfg::LT - 1) / Cfg::LT;
+    prm.nstage = nstage;
+    CUtensorMap maps[4];
+    memset(maps, 0, sizeof(maps));
+    const int dts[4] = {
+        (K == Kind::RevPlain) ? call.te : call.tin,
+        (K == Kind::RevPlain) ? call.te : call.tin,
+        call.te,
+        call.te,
+    };
+    for (int a = 0; a < P::NIN; ++a) {
+        std::string err;
+        const int64_t rs = call.a.in[a].rs;
+        if (!encode_strip_map(&maps[a], dts[a], call.a.in[a].p, call.a.nb, call.a.T, call.a.hd, rs,
+                              Cfg::WS, Cfg::LT, &err))
+            return set_error(ESA_ERR_CUDA, "tensor map: " + err);
+    }
+    const size_t smem = Cfg::smem_bytes(nstage);
+    cudaError_t e = cudaFuncSetAttribute(strip_scan_kernel<K, Tin, Te, LPR, SR>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("strip smem attribute: ") + cudaGetErrorString(e));
+    if (grid > prm.nitems) grid = (int)prm.nitems;
+    strip_scan_kernel<K, Tin, Te, LPR, SR><<<grid, Cfg::NT, smem, call.stream>>>(prm, maps[0], maps[1],
+                                                                                  maps[2], maps[3]);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("strip scan launch: ") + cudaGetErrorString(e));
+    return ESA_OK;
+}
+
+// Occupancy (CTAs per SM) of a strip configuration with `nstage` stages
+// (cached per device and stage count; 0 if it cannot be resident).
+template <Kind K, typename Tin, typename Te, int LPR, int SR>
+int strip_occupancy(int dev, int nstage) {
+    using Cfg = StripCfg<K, Tin, Te, LPR, SR>;
+    static int cache[16][9];  // [device][nstage]: 0 unknown, -1 none, else occupancy
+    if (dev < 0 || dev >= 16 || nstage < 1 || nstage > 8) return 0;
+    int& slot = cache[dev][nstage];
+    if (slot != 0) return slot < 0 ? 0 : slot;
+    const size_t smem = Cfg::smem_bytes(nstage);
+    int per_sm = 0;
+    if (smem <= 232448 &&
+        cudaFuncSetAttribute(strip_scan_kernel<K, Tin, Te, LPR, SR>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, strip_scan_kernel<K, Tin, Te, LPR, SR>,
+                                                      Cfg::NT, smem) == cudaSuccess &&
+        per_sm > 0) {
+        slot = per_sm;
+    } else {
+        slot = -1;
+        per_sm = 0;
+    }
+    return per_sm;
+}
+
+// Picks the strip width (LPR) and pipeline depth for the call, or declines
+// (*taken = false) when the strips cannot fill the GPU (then the caller uses
+// the time-parallel lookback scan).  Preference order:
+//   1. every strip resident in one wave (no tail wave) with >= 3 stages;
+//   2. the same with 2 stages;
+//   3. the widest strips (longest DRAM rows, fewest CTAs) among those.
+template <Kind K, typename Tin, typename Te, int SR4, int SR8, int SR16, int SR32>
+int strip_launch_kind(const ScanCall& call, bool* taken) {
+    *taken = false;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = device_sm_count(dev);
+    const int64_t T = call.a.T, nb = call.a.nb, hd = call.a.hd;
+    using P = Policy<K, Tin, Te>;
+    if (T < 16) return ESA_OK;
+    auto strips = [&](int lpr) { return nb * ((hd + lpr * P::VEC - 1) / (lpr * P::VEC)); };
+    auto occ = [&](int lpr, int ns) -> int {
+        switch (lpr) {
+            case 32: return strip_occupancy<K, Tin, Te, 32, SR32>(dev, ns);
+            case 16: return strip_occupancy<K, Tin, Te, 16, SR16>(dev, ns);
+            case 8: return strip_occupancy<K, Tin, Te, 8, SR8>(dev, ns);
+            default: return strip_occupancy<K, Tin, Te, 4, SR4>(dev, ns);
+        }
+    };
+    int pick_lpr = 0, pick_ns = 0, pick_occ = 0;
+    for (int min_ns = 3; min_ns >= 2 && pick_lpr == 0; --min_ns) {
+        for (int lpr : {32, 16, 8, 4}) {
+            const int64_t n = strips(lpr);
+            if (n < (sms * 3) / 4) continue;  // too few strips to fill the GPU
+            for (int ns = 6; ns >= min_ns; --ns) {
+                const int o = occ(lpr, ns);
+                if (o > 0 && (int64_t)o * sms >= n) {
+                    pick_lpr = lpr;
+                    pick_ns = ns;
+                    pick_occ = o;
+                    break;
+                }
+            }
+            if (pick_lpr) break;
+        }
+    }
+    if (pick_lpr == 0) {
+        // more strips than can be resident at once: 2 stages, persistent CTAs
+        for (int lpr : {8, 16, 32, 4}) {
+            const int o = occ(lpr, 2);
+            if (strips(lpr) >= (sms * 3) / 4 && o > 0) {
+                pick_lpr = lpr;
+                pick_ns = 2;
+                pick_occ = o;
+                break;
+            }
+        }
+    }
+    if (pick_lpr == 0) return ESA_OK;  // too few channels for strips: not taken
+    *taken = true;
+    const int64_t n = strips(pick_lpr);
+    const int64_t cap = (int64_t)pick_occ * sms;
+    const int grid = (int)(n < cap ? n : cap);
+    switch (pick_lpr) {
+        case 32: return strip_launch_typed<K, Tin, Te, 32, SR32>(call, pick_ns, grid);
+        case 16: return strip_launch_typed<K, Tin, Te, 16, SR16>(call, pick_ns, grid);
+        case 8: return strip_launch_typed<K, Tin, Te, 8, SR8>(call, pick_ns, grid);
+        default: return strip_launch_typed<K, Tin, Te, 4, SR4>(call, pick_ns, grid);
+    }
+}
+
+}  // namespace esa

@@ -28,7 +28,7 @@ _lib = None
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
-_f32 = ctypes.c_float
+_f64 = ctypes.c_double
 _sz = ctypes.c_size_t
 
 # name -> (restype, argtypes); the exact set of symbols include/esa_b200.h declares
@@ -40,13 +40,13 @@ SIGNATURES = {
     "esa_scan_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _sz, _vp]),
     "esa_scan_rev": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp,
                             _sz, _vp]),
-    "esa_gated_scan_fwd": (_int, [_vp, _vp, _i64, _int, _vp, _int, _i64, _i64, _i64, _f32, _f32,
+    "esa_gated_scan_fwd": (_int, [_vp, _vp, _i64, _int, _vp, _int, _i64, _i64, _i64, _f64, _f64,
                                   _int, _int, _vp, _vp, _vp, _sz, _vp]),
     "esa_gated_scan_bwd": (_int, [_vp, _vp, _i64, _int, _vp, _vp, _int, _vp, _vp, _i64, _int,
-                                  _i64, _i64, _i64, _f32, _f32, _int, _int, _vp, _vp, _vp, _sz,
+                                  _i64, _i64, _i64, _f64, _f64, _int, _int, _vp, _vp, _vp, _sz,
                                   _vp]),
-    "esa_lightning_step": (_int, [_vp, _i64, _int, _vp, _vp, _int, _vp, _int, _i64, _i64, _f32,
-                                  _f32, _f32, _vp]),
+    "esa_lightning_step": (_int, [_vp, _i64, _int, _vp, _vp, _int, _vp, _int, _i64, _i64, _f64,
+                                  _f64, _f64, _vp]),
 }
 
 

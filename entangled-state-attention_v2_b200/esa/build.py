@@ -1,9 +1,11 @@
 """Build libesa_b200.so in-tree with nvcc for sm_100a (no JIT cache).
 
-    python -m esa.build          (from entangled-state-attention_v2_b200/)
+    python -m esa.build [--force]      (from entangled-state-attention_v2_b200/)
 
-Sources: ../csrc/*.cu.  cudart is linked statically so the library carries no
-runtime-version coupling to the PyTorch wheel's own cudart.
+Sources: ../csrc/*.cu, compiled to objects in parallel (one nvcc per
+translation unit) and linked into esa/libesa_b200.so.  cudart is linked
+statically so the library carries no runtime-version coupling to the PyTorch
+wheel's own cudart.
 """
 
 from __future__ import annotations
@@ -12,14 +14,17 @@ import os
 import shutil
 import subprocess
 import sys
+import tempfile
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
+INCLUDE = PKG.parent.parent / "include"
 OUT = PKG / "libesa_b200.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-         "--expt-relaxed-constexpr", "-cudart", "static"]
+CFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+          "-Xcompiler", "-fvisibility=hidden"]
 
 
 def nvcc() -> str:
@@ -38,23 +43,40 @@ def up_to_date() -> bool:
         return False
     t = OUT.stat().st_mtime
     deps = sources() + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + \
-        [PKG.parent.parent / "include" / "esa_b200.h", Path(__file__)]
+        [INCLUDE / "esa_b200.h", Path(__file__)]
     return all(p.stat().st_mtime <= t for p in deps if p.exists())
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and up_to_date():
-        return OUT
-    tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, *FLAGS, "-o", str(tmp), *map(str, sources())]
-    if verbose:
-        print(" ".join(cmd))
-    # compile translation units in parallel
-    subprocess.run(cmd + ["--threads", "0"], check=True)
-    os.replace(tmp, OUT)
-    return OUT
+def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None,
+          out: Path | None = None) -> Path:
+    out = out or OUT
+    if not force and out == OUT and up_to_date():
+        return out
+    exe = nvcc()
+    flags = CFLAGS + list(extra_flags or [])
+    with tempfile.TemporaryDirectory(prefix="esa_build_") as tmp:
+        objs = []
+
+        def compile_one(src: Path) -> Path:
+            obj = Path(tmp) / (src.stem + ".o")
+            cmd = [exe, *ARCH, *flags, "-c", str(src), "-o", str(obj)]
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            subprocess.run(cmd, check=True)
+            return obj
+
+        with ThreadPoolExecutor(max_workers=max(1, min(len(sources()), os.cpu_count() or 1))) as ex:
+            objs = list(ex.map(compile_one, sources()))
+        tmp_out = Path(tmp) / out.name
+        cmd = [exe, *ARCH, "-shared", "-cudart", "static", "-o", str(tmp_out), *map(str, objs)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+        shutil.copyfile(tmp_out, str(out) + ".tmp")
+        os.replace(str(out) + ".tmp", out)
+    return out
 
 
 if __name__ == "__main__":
-    build(force="--force" in sys.argv, verbose=True)
+    build(force="--force" in sys.argv, verbose="-v" in sys.argv)
     print(OUT)

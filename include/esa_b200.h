@@ -19,8 +19,11 @@
  *     gives a message (thread-local).  Failures detected on the device (a wait
  *     that ran past its one-second budget) are OR-ed into a per-device status
  *     word read by esa_device_status().
- *   - "acc" type: float for f16/bf16/f32 data, double for f64 data.  Initial
+ *   - "acc" type: double if any tensor of the call is f64, else float.  Initial
  *     and final states (e0, e_last, de0) use the acc type, shape [nb, hd].
+ *   - gate_min, gate_max, eps are doubles; kernels use (acc)gate_min and
+ *     (acc)(gate_max - gate_min), the values PyTorch uses for
+ *     `gate_min + (gate_max - gate_min) * sigmoid(g)` with Python-float bounds.
  */
 #ifndef ESA_B200_H
 #define ESA_B200_H
@@ -101,7 +104,7 @@ int esa_scan_rev(const void *A, const void *E, const void *dE, void *dA, void *d
  * thunder_scan) and generation.py:439-445 + :476-487 (prefill). */
 int esa_gated_scan_fwd(const void *gate_raw, const void *value_raw, int64_t raw_row_stride,
                        int raw_dtype, void *E, int e_dtype, int64_t nb, int64_t T, int64_t hd,
-                       float gate_min, float gate_max, int round_ab, int compass, const void *e0,
+                       double gate_min, double gate_max, int round_ab, int compass, const void *e0,
                        void *e_last, void *workspace, size_t workspace_bytes, void *stream);
 
 /* Backward of esa_gated_scan_fwd, fused: reverse scan plus the gate chain rule
@@ -114,8 +117,8 @@ int esa_gated_scan_fwd(const void *gate_raw, const void *value_raw, int64_t raw_
 int esa_gated_scan_bwd(const void *gate_raw, const void *value_raw, int64_t raw_row_stride,
                        int raw_dtype, const void *E, const void *dE, int e_dtype,
                        void *d_gate_raw, void *d_value_raw, int64_t draw_row_stride,
-                       int draw_dtype, int64_t nb, int64_t T, int64_t hd, float gate_min,
-                       float gate_max, int round_ab, int compass, const void *e0, void *de0,
+                       int draw_dtype, int64_t nb, int64_t T, int64_t hd, double gate_min,
+                       double gate_max, int round_ab, int compass, const void *e0, void *de0,
                        void *workspace, size_t workspace_bytes, void *stream);
 
 /* One ESA-Lightning decode step for nb rows, fused: gate nonlinearity, state
@@ -128,8 +131,8 @@ int esa_gated_scan_bwd(const void *gate_raw, const void *value_raw, int64_t raw_
  * A S + B, _readout up to out_proj; _readout is generation.py:270-293). */
 int esa_lightning_step(const void *qgv, int64_t qgv_row_stride, int qgv_dtype,
                        const void *state, void *new_state, int state_dtype, void *z,
-                       int z_dtype, int64_t nb, int64_t C, float gate_min, float gate_max,
-                       float eps, void *stream);
+                       int z_dtype, int64_t nb, int64_t C, double gate_min, double gate_max,
+                       double eps, void *stream);
 
 #ifdef __cplusplus
 }

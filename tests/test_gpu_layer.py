@@ -72,8 +72,9 @@ def test_layer_half_precision_scan(precision, scan_dtype):
     ref = oracle.scan_fwd(Ar, Br).reshape(2, 96, 128)
     assert rel(E, ref) < 2e-3
     y = lay(x)
-    y64 = oracle.pulse_layer_forward(torch.from_numpy(z["x"]), torch.from_numpy(z["qgv_w"]),
-                                     torch.from_numpy(z["out_w"]), head=4)
+    y64 = oracle.pulse_layer_forward(torch.from_numpy(z["x"]).double(),
+                                     torch.from_numpy(z["qgv_w"]).double(),
+                                     torch.from_numpy(z["out_w"]).double(), head=4)
     assert rel(y, y64) < 2e-2  # includes the A/B rounding to 16 bits, as in the reference
 
 
