@@ -83,6 +83,25 @@ int esa_scan_fwd(const void *A, const void *B, void *E, int64_t nb, int64_t T, i
                  int dtype, int compass, const void *e0, void *e_last, void *workspace,
                  size_t workspace_bytes, void *stream);
 
+/* Scratch size of esa_scan_fwd_noalloc (bytes). */
+#define ESA_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* esa_scan_fwd for callers that cannot allocate device memory -- e.g. a C
+ * host program or a foreign-language binding that receives its input and
+ * output buffers from elsewhere, or code whose device memory plan is fixed
+ * before it runs.  Same arguments and results as esa_scan_fwd, without the
+ * workspace: the time-parallel scan kernel takes its scratch from a fixed
+ * array of ESA_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that
+ * loads the library holds until the process exits.  Problems whose scratch
+ * would exceed that size are rejected with ESA_ERR_WORKSPACE and a message.
+ * The first call on each device looks the array's address up
+ * (cudaGetSymbolAddress); make it before any stream capture.  All calls share
+ * the array, so calls that overlap on the GPU (e.g. on two streams at once)
+ * race.  No counterpart in the reference: it has no native code and no
+ * allocator-free interface. */
+int esa_scan_fwd_noalloc(const void *A, const void *B, void *E, int64_t nb, int64_t T, int64_t hd,
+                         int dtype, int compass, const void *e0, void *e_last, void *stream);
+
 /* Reverse-time scan: the gradient of esa_scan_fwd.
  *   G_t = dE_t + A_{t+1} G_{t+1};  dB_t = G_t;  dA_t = G_t * E_{t-1}
  * with E_{-1} = e0 (NULL: zero); de0 (nullable) receives A_0 * G_0, the
