@@ -70,27 +70,145 @@ struct Policy {
     static __host__ __device__ constexpr int shift(int i) {
         return (K == Kind::RevPlain && i == 1) || (K == Kind::RevGated && i == 2) ? -1 : 0;
     }
-    // phase-1 values kept in registers for phase 3 (S rows x VEC channels)
+    // element size of the outputs (E, dA/dB: Te; d gate/d value: Tin)
+    static constexpr int OES = (K == Kind::RevGated) ? (int)sizeof(Tin) : (int)sizeof(Te);
+    // phase-1 values kept in registers for phase 3 (S rows x VEC channels):
+    // forward: (A, B); reverse: (A or sigmoid(g), dE).  Phase 3 then needs no
+    // shared-memory reload or conversion of them.
     template <int S>
     struct Cache {
-        acc c0[S][GATED ? VEC : 1];
-        acc c1[S][(K == Kind::FwdGated) ? VEC : 1];
+        acc c0[S][VEC];
+        acc c1[S][VEC];
     };
 };
 
+// ---------------------------------------------------------------------------
+// Lane-vector arithmetic.  fp32 vectors use Blackwell's packed two-lane FP32
+// instructions (__ffma2_rn / __fmul2_rn / __fadd2_rn: one instruction per
+// channel pair, IEEE round-to-nearest per lane, the same results as scalar
+// fmaf/__fmul_rn/__fadd_rn); fp64 vectors use scalar instructions.
+// ---------------------------------------------------------------------------
+// d = a * b + c
+template <int N>
+__device__ __forceinline__ void vfma(float (&d)[N], const float (&a)[N], const float (&b)[N],
+                                     const float (&c)[N]) {
+    static_assert(N % 2 == 0, "pairs");
+#pragma unroll
+    for (int i = 0; i < N; i += 2) {
+        const float2 r = __ffma2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]),
+                                   make_float2(c[i], c[i + 1]));
+        d[i] = r.x;
+        d[i + 1] = r.y;
+    }
+}
+template <int N>
+__device__ __forceinline__ void vfma(double (&d)[N], const double (&a)[N], const double (&b)[N],
+                                     const double (&c)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) d[i] = fma(a[i], b[i], c[i]);
+}
+// d = a * b
+template <int N>
+__device__ __forceinline__ void vmul(float (&d)[N], const float (&a)[N], const float (&b)[N]) {
+    static_assert(N % 2 == 0, "pairs");
+#pragma unroll
+    for (int i = 0; i < N; i += 2) {
+        const float2 r = __fmul2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]));
+        d[i] = r.x;
+        d[i + 1] = r.y;
+    }
+}
+template <int N>
+__device__ __forceinline__ void vmul(double (&d)[N], const double (&a)[N], const double (&b)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) d[i] = a[i] * b[i];
+}
+// d = a + b
+template <int N>
+__device__ __forceinline__ void vadd(float (&d)[N], const float (&a)[N], const float (&b)[N]) {
+    static_assert(N % 2 == 0, "pairs");
+#pragma unroll
+    for (int i = 0; i < N; i += 2) {
+        const float2 r = __fadd2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]));
+        d[i] = r.x;
+        d[i + 1] = r.y;
+    }
+}
+template <int N>
+__device__ __forceinline__ void vadd(double (&d)[N], const double (&a)[N], const double (&b)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) d[i] = a[i] + b[i];
+}
+// Compose the affine pair (qa, qb) (earlier) with (pa, pb) (later):
+// (pa, pb) <- (pa*qa, pa*qb + pb).
+template <typename A, int N>
+__device__ __forceinline__ void vcompose(A (&pa)[N], A (&pb)[N], const A (&qa)[N], const A (&qb)[N]) {
+    vfma(pb, pa, qb, pb);
+    vmul(pa, pa, qa);
+}
+
+// Load N elements of T from shared memory and widen them to the accumulator
+// type (16-bit types in pairs: one conversion per channel pair).
 template <typename T, int N, typename A>
 __device__ __forceinline__ void load_smem(const char* p, A (&out)[N]) {
-    VecN<T, N> v = *reinterpret_cast<const VecN<T, N>*>(p);
+    if constexpr (std::is_same<T, __half>::value && std::is_same<A, float>::value && N % 2 == 0) {
+        const VecN<__half2, N / 2> v = *reinterpret_cast<const VecN<__half2, N / 2>*>(p);
 #pragma unroll
-    for (int i = 0; i < N; ++i) out[i] = static_cast<A>(Elem<T>::to_acc(v.v[i]));
+        for (int i = 0; i < N / 2; ++i) {
+            const float2 f = __half22float2(v.v[i]);
+            out[2 * i] = f.x;
+            out[2 * i + 1] = f.y;
+        }
+    } else if constexpr (std::is_same<T, __nv_bfloat16>::value && std::is_same<A, float>::value && N % 2 == 0) {
+        const VecN<__nv_bfloat162, N / 2> v = *reinterpret_cast<const VecN<__nv_bfloat162, N / 2>*>(p);
+#pragma unroll
+        for (int i = 0; i < N / 2; ++i) {
+            const float2 f = __bfloat1622float2(v.v[i]);
+            out[2 * i] = f.x;
+            out[2 * i + 1] = f.y;
+        }
+    } else {
+        VecN<T, N> v = *reinterpret_cast<const VecN<T, N>*>(p);
+#pragma unroll
+        for (int i = 0; i < N; ++i) out[i] = static_cast<A>(Elem<T>::to_acc(v.v[i]));
+    }
+}
+
+// Vector load / store of N accumulators (one thread's channels) in shared
+// memory: a warp touches one contiguous span, so no bank conflicts beyond the
+// span's width.
+template <typename A, int N>
+__device__ __forceinline__ void lds_vec(const A* p, A (&out)[N]) {
+    const VecN<A, N> v = *reinterpret_cast<const VecN<A, N>*>(p);
+#pragma unroll
+    for (int i = 0; i < N; ++i) out[i] = v.v[i];
+}
+template <typename A, int N>
+__device__ __forceinline__ void sts_vec(A* p, const A (&in)[N]) {
+    VecN<A, N> v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) v.v[i] = in[i];
+    *reinterpret_cast<VecN<A, N>*>(p) = v;
 }
 
 template <typename T, int N, typename A>
 __device__ __forceinline__ void store_global(char* p, const A (&in)[N]) {
-    VecN<T, N> v;
+    if constexpr (std::is_same<T, __half>::value && std::is_same<A, float>::value && N % 2 == 0) {
+        VecN<__half2, N / 2> v;
 #pragma unroll
-    for (int i = 0; i < N; ++i) v.v[i] = Elem<T>::from_acc(static_cast<typename Elem<T>::acc>(in[i]));
-    *reinterpret_cast<VecN<T, N>*>(p) = v;
+        for (int i = 0; i < N / 2; ++i) v.v[i] = __floats2half2_rn(in[2 * i], in[2 * i + 1]);
+        *reinterpret_cast<VecN<__half2, N / 2>*>(p) = v;
+    } else if constexpr (std::is_same<T, __nv_bfloat16>::value && std::is_same<A, float>::value && N % 2 == 0) {
+        VecN<__nv_bfloat162, N / 2> v;
+#pragma unroll
+        for (int i = 0; i < N / 2; ++i) v.v[i] = __floats2bfloat162_rn(in[2 * i], in[2 * i + 1]);
+        *reinterpret_cast<VecN<__nv_bfloat162, N / 2>*>(p) = v;
+    } else {
+        VecN<T, N> v;
+#pragma unroll
+        for (int i = 0; i < N; ++i) v.v[i] = Elem<T>::from_acc(static_cast<typename Elem<T>::acc>(in[i]));
+        *reinterpret_cast<VecN<T, N>*>(p) = v;
+    }
 }
 
 // Per-step coefficients (a, b) of step row `rows` (phase 1).  `rows[i]` points
@@ -105,6 +223,11 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
     if constexpr (K == Kind::FwdPlain) {
         load_smem<Tin, VEC>(rows[0], a);
         load_smem<Tin, VEC>(rows[1], b);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+            cache.c0[s][i] = a[i];
+            cache.c1[s][i] = b[i];
+        }
     } else if constexpr (K == Kind::FwdGated) {
         acc g[VEC], v[VEC];
         load_smem<Tin, VEC>(rows[0], g);
@@ -128,7 +251,11 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
         load_smem<Te, VEC>(rows[0], a);
         load_smem<Te, VEC>(rows[2], d);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) b[i] = a[i] * d[i];
+        for (int i = 0; i < VEC; ++i) {
+            b[i] = a[i] * d[i];
+            cache.c0[s][i] = a[i];
+            cache.c1[s][i] = d[i];
+        }
     } else {  // RevGated
         acc g[VEC], d[VEC];
         load_smem<Tin, VEC>(rows[0], g);
@@ -140,6 +267,7 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
             acc A = lo + span * sg;
             if (prm.round_ab) A = round_to<Te>(A);
             cache.c0[s][i] = sg;
+            cache.c1[s][i] = d[i];
             a[i] = A;
             b[i] = A * d[i];
         }
@@ -153,26 +281,22 @@ template <Kind K, typename Tin, typename Te, int S, typename P = Policy<K, Tin, 
 __device__ __forceinline__ void step_apply(const char* const (&rows)[4], const KArgs& prm,
                                            int64_t b, int64_t t, int64_t gc, bool valid,
                                            typename P::acc (&e)[P::VEC],
-                                           typename P::template Cache<S>& cache, int s) {
+                                           typename P::template Cache<S>& cache, int s, char* o0,
+                                           char* o1) {
     using acc = typename P::acc;
     constexpr int VEC = P::VEC;
-    const int64_t orow = b * prm.T + t;
     if constexpr (K == Kind::FwdPlain) {
-        acc a[VEC], bb[VEC];
-        load_smem<Tin, VEC>(rows[0], a);
-        load_smem<Tin, VEC>(rows[1], bb);
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) e[i] = a[i] * e[i] + bb[i];
+        vfma(e, cache.c0[s], e, cache.c1[s]);
         if (valid)
-            store_global<Te, VEC>(prm.out[0].p + (orow * prm.out[0].rs + gc) * (int64_t)sizeof(Te), e);
+            store_global<Te, VEC>(o0, e);
     } else if constexpr (K == Kind::FwdGated) {
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) e[i] = cache.c0[s][i] * e[i] + cache.c1[s][i];
+        vfma(e, cache.c0[s], e, cache.c1[s]);
         if (valid)
-            store_global<Te, VEC>(prm.out[0].p + (orow * prm.out[0].rs + gc) * (int64_t)sizeof(Te), e);
+            store_global<Te, VEC>(o0, e);
     } else {
         acc ep[VEC], d[VEC];
-        load_smem<Te, VEC>(K == Kind::RevPlain ? rows[2] : rows[3], d);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) d[i] = cache.c1[s][i];
         if (t > 0) {
             load_smem<Te, VEC>(K == Kind::RevPlain ? rows[1] : rows[2], ep);
         } else {
@@ -185,18 +309,13 @@ __device__ __forceinline__ void step_apply(const char* const (&rows)[4], const K
             }
         }
         if constexpr (K == Kind::RevPlain) {
-            acc a[VEC], ga[VEC];
-            load_smem<Te, VEC>(rows[0], a);
-#pragma unroll
-            for (int i = 0; i < VEC; ++i) {
-                const acc g = d[i] + e[i];
-                ga[i] = g * ep[i];
-                d[i] = g;  // dB
-                e[i] = a[i] * g;
-            }
+            acc ga[VEC];
+            vadd(d, d, e);            // G_t = dE_t + H_{t+1}  (= dB)
+            vmul(ga, d, ep);          // dA = G_t E_{t-1}
+            vmul(e, cache.c0[s], d);  // H_t = A_t G_t
             if (valid) {
-                store_global<Te, VEC>(prm.out[0].p + (orow * prm.out[0].rs + gc) * (int64_t)sizeof(Te), ga);
-                store_global<Te, VEC>(prm.out[1].p + (orow * prm.out[1].rs + gc) * (int64_t)sizeof(Te), d);
+                store_global<Te, VEC>(o0, ga);
+                store_global<Te, VEC>(o1, d);
             }
         } else {
             acc v[VEC], dg[VEC], dv[VEC];
@@ -215,8 +334,8 @@ __device__ __forceinline__ void step_apply(const char* const (&rows)[4], const K
                 e[i] = Ar * g;
             }
             if (valid) {
-                store_global<Tin, VEC>(prm.out[0].p + (orow * prm.out[0].rs + gc) * (int64_t)sizeof(Tin), dg);
-                store_global<Tin, VEC>(prm.out[1].p + (orow * prm.out[1].rs + gc) * (int64_t)sizeof(Tin), dv);
+                store_global<Tin, VEC>(o0, dg);
+                store_global<Tin, VEC>(o1, dv);
             }
         }
     }

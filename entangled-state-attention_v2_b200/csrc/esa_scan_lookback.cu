@@ -412,7 +412,11 @@ __global__ void __launch_bounds__(512) lookback_scan_kernel(const LbParams prm) 
                 if (t < ka.T) {
                     const char* rows[4];
                     row_ptrs(r, rows);
-                    step_apply<K, Tin, Te, S>(rows, ka, tc.b, t, tc.cb + c, valid, e, cache, s);
+                    const int64_t orow = tc.b * ka.T + t;
+                    step_apply<K, Tin, Te, S>(
+                        rows, ka, tc.b, t, tc.cb + c, valid, e, cache, s,
+                        ka.out[0].p + (orow * ka.out[0].rs + tc.cb + c) * (int64_t)P::OES,
+                        ka.out[1].p + (orow * ka.out[1].rs + tc.cb + c) * (int64_t)P::OES);
                 }
             }
             // reverse: H_0 = A_0 G_0 is the gradient w.r.t. the initial state

@@ -32,6 +32,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -95,8 +96,34 @@ __device__ __forceinline__ void strip_issue(const StripParams& prm, const CUtens
                     (int)(t0 + P::shift(a)), (int)b, bar, policy);
 }
 
+// A shared-memory row of one accumulator vector per lane (LPR lanes x N
+// accumulators), stored planar: plane p holds every lane's p-th 16-byte chunk,
+// so a warp-wide access to one plane is a contiguous span (no bank conflicts
+// beyond its width, whatever N is).
+template <typename A, int N, int LPR>
+__device__ __forceinline__ void lds_planar(const A* row, int cl, A (&out)[N]) {
+    constexpr int PER = 16 / (int)sizeof(A);
+#pragma unroll
+    for (int p = 0; p < N / PER; ++p) {
+        const VecN<A, PER> v = *reinterpret_cast<const VecN<A, PER>*>(row + (p * LPR + cl) * PER);
+#pragma unroll
+        for (int i = 0; i < PER; ++i) out[p * PER + i] = v.v[i];
+    }
+}
+template <typename A, int N, int LPR>
+__device__ __forceinline__ void sts_planar(A* row, int cl, const A (&in)[N]) {
+    constexpr int PER = 16 / (int)sizeof(A);
+#pragma unroll
+    for (int p = 0; p < N / PER; ++p) {
+        VecN<A, PER> v;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) v.v[i] = in[p * PER + i];
+        *reinterpret_cast<VecN<A, PER>*>(row + (p * LPR + cl) * PER) = v;
+    }
+}
+
 template <Kind K, typename Tin, typename Te, int LPR, int SR>
-__global__ void __launch_bounds__(256) strip_scan_kernel(const StripParams prm,
+__global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams prm,
                                                          const __grid_constant__ CUtensorMap m0,
                                                          const __grid_constant__ CUtensorMap m1,
                                                          const __grid_constant__ CUtensorMap m2,
@@ -115,6 +142,7 @@ __global__ void __launch_bounds__(256) strip_scan_kernel(const StripParams prm,
 
     extern __shared__ __align__(128) char smem_raw[];
     char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    // per-warp tile aggregates [NW][WS]
     acc* wagg_a = reinterpret_cast<acc*>(smem + (size_t)nstage * Cfg::stage_bytes());
     acc* wagg_b = wagg_a + NW * WS;
     acc* carry = wagg_b + NW * WS;  // [2][WS], double-buffered by tile parity
@@ -151,12 +179,12 @@ __global__ void __launch_bounds__(256) strip_scan_kernel(const StripParams prm,
         };
         // initial carry: e0 (forward) or zero (reverse: nothing after T)
         if (rgl == 0 && warp == 0) {
+            acc x[VEC];
 #pragma unroll
-            for (int i = 0; i < VEC; ++i) {
-                acc x = acc(0);
-                if (!P::REV && ka.e0 != nullptr && valid) x = static_cast<const acc*>(ka.e0)[b * ka.hd + gc + i];
-                carry[c + i] = x;  // slot 0
-            }
+            for (int i = 0; i < VEC; ++i)
+                x[i] = (!P::REV && ka.e0 != nullptr && valid) ? static_cast<const acc*>(ka.e0)[b * ka.hd + gc + i]
+                                                              : acc(0);
+            sts_planar<acc, VEC, LPR>(carry, cl, x);  // slot 0
         }
         // prologue: fill the ring
         const int npro = (int)(prm.ntt < nstage ? prm.ntt : nstage);
@@ -201,62 +229,66 @@ __global__ void __launch_bounds__(256) strip_scan_kernel(const StripParams prm,
                     rows_at(r, rows);
                     acc a[VEC], bb[VEC];
                     step_coef<K, Tin, Te, SR>(rows, ka, a, bb, cache, s);
-#pragma unroll
-                    for (int i = 0; i < VEC; ++i) {
-                        pb[i] = a[i] * pb[i] + bb[i];
-                        pa[i] = a[i] * pa[i];
-                    }
+                    vfma(pb, a, pb, bb);
+                    vmul(pa, a, pa);
                 }
             }
             // ---- warp: inclusive scan over row groups (shuffles) -----------
+            acc ex_a[VEC], ex_b[VEC];  // first round's neighbour (RGW == 2: the exclusive prefix)
 #pragma unroll
             for (int d = 1; d < RGW; d <<= 1) {
+                acc qa[VEC], qb[VEC];
+                const bool take = P::REV ? (rgl + d < RGW) : (rgl >= d);
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) {
-                    acc qa, qb;
                     if constexpr (P::REV) {
-                        qa = __shfl_down_sync(FULL, pa[i], d * LPR);
-                        qb = __shfl_down_sync(FULL, pb[i], d * LPR);
+                        qa[i] = __shfl_down_sync(FULL, pa[i], d * LPR);
+                        qb[i] = __shfl_down_sync(FULL, pb[i], d * LPR);
                     } else {
-                        qa = __shfl_up_sync(FULL, pa[i], d * LPR);
-                        qb = __shfl_up_sync(FULL, pb[i], d * LPR);
+                        qa[i] = __shfl_up_sync(FULL, pa[i], d * LPR);
+                        qb[i] = __shfl_up_sync(FULL, pb[i], d * LPR);
                     }
-                    const bool take = P::REV ? (rgl + d < RGW) : (rgl >= d);
-                    if (take) {
-                        pb[i] = pa[i] * qb + pb[i];
-                        pa[i] = pa[i] * qa;
+                    if (d == 1) {
+                        ex_a[i] = qa[i];
+                        ex_b[i] = qb[i];
                     }
+                    // lanes without an earlier row group compose with identity
+                    qa[i] = take ? qa[i] : acc(1);
+                    qb[i] = take ? qb[i] : acc(0);
                 }
+                vcompose(pa, pb, qa, qb);
             }
-            // exclusive prefix of this row group within the warp
+            // exclusive prefix of this row group within the warp (with two row
+            // groups it is the first round's shuffled value)
             acc xa[VEC], xb[VEC];
-#pragma unroll
-            for (int i = 0; i < VEC; ++i) {
-                acc qa, qb;
-                if constexpr (RGW > 1) {
-                    if constexpr (P::REV) {
-                        qa = __shfl_down_sync(FULL, pa[i], LPR);
-                        qb = __shfl_down_sync(FULL, pb[i], LPR);
-                    } else {
-                        qa = __shfl_up_sync(FULL, pa[i], LPR);
-                        qb = __shfl_up_sync(FULL, pb[i], LPR);
-                    }
-                } else {
-                    qa = acc(1);
-                    qb = acc(0);
-                }
+            {
                 const bool first = P::REV ? (rgl == RGW - 1) : (rgl == 0);
-                xa[i] = first ? acc(1) : qa;
-                xb[i] = first ? acc(0) : qb;
-            }
-            if (last_rgl) {
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) {
-                    wagg_a[warp * WS + c + i] = pa[i];
-                    wagg_b[warp * WS + c + i] = pb[i];
+                    acc qa = acc(1), qb = acc(0);
+                    if constexpr (RGW == 2) {
+                        qa = ex_a[i];
+                        qb = ex_b[i];
+                    } else if constexpr (RGW > 1) {
+                        if constexpr (P::REV) {
+                            qa = __shfl_down_sync(FULL, pa[i], LPR);
+                            qb = __shfl_down_sync(FULL, pb[i], LPR);
+                        } else {
+                            qa = __shfl_up_sync(FULL, pa[i], LPR);
+                            qb = __shfl_up_sync(FULL, pb[i], LPR);
+                        }
+                    }
+                    xa[i] = first ? acc(1) : qa;
+                    xb[i] = first ? acc(0) : qb;
                 }
             }
-            __syncthreads();
+            acc* const wa = wagg_a;
+            acc* const wb = wagg_b;
+            if (last_rgl) {
+                sts_planar<acc, VEC, LPR>(wa + warp * WS, cl, pa);
+                sts_planar<acc, VEC, LPR>(wb + warp * WS, cl, pb);
+            }
+            __syncthreads();  // warp totals of this tile visible
 
             // ---- CTA: exclusive prefix over the warps before this one -------
             acc ea[VEC], eb[VEC];
@@ -269,21 +301,22 @@ __global__ void __launch_bounds__(256) strip_scan_kernel(const StripParams prm,
             for (int n = 0; n < NW; ++n) {
                 const int w = P::REV ? (NW - 1 - n) : n;
                 if (w == warp) break;
-#pragma unroll
-                for (int i = 0; i < VEC; ++i) {
-                    const acc aw = wagg_a[w * WS + c + i];
-                    const acc bw = wagg_b[w * WS + c + i];
-                    eb[i] = aw * eb[i] + bw;
-                    ea[i] = aw * ea[i];
-                }
+                acc aw[VEC], bw[VEC];
+                lds_planar<acc, VEC, LPR>(wa + w * WS, cl, aw);
+                lds_planar<acc, VEC, LPR>(wb + w * WS, cl, bw);
+                vfma(eb, aw, eb, bw);
+                vmul(ea, aw, ea);
             }
             // ---- phase 3: incoming state, re-run, outputs ------------------
             acc e[VEC];
-#pragma unroll
-            for (int i = 0; i < VEC; ++i) {
-                const acc x = ea[i] * carry[cur * WS + c + i] + eb[i];
-                e[i] = xa[i] * x + xb[i];
-            }
+            lds_planar<acc, VEC, LPR>(carry + cur * WS, cl, e);
+            vfma(e, ea, e, eb);  // through the warps before this one
+            vfma(e, xa, e, xb);  // through the row groups before this one
+            // output addresses of this row group's first step; one row stride per step
+            const int64_t orow0 = b * ka.T + t0 + rg * SR;
+            char* const ob0 = ka.out[0].p + (orow0 * ka.out[0].rs + gc) * (int64_t)P::OES;
+            char* const ob1 = ka.out[1].p + (orow0 * ka.out[1].rs + gc) * (int64_t)P::OES;
+            const int64_t os0 = ka.out[0].rs * (int64_t)P::OES, os1 = ka.out[1].rs * (int64_t)P::OES;
 #pragma unroll
             for (int ss = 0; ss < SR; ++ss) {
                 const int s = P::REV ? (SR - 1 - ss) : ss;
@@ -292,13 +325,11 @@ __global__ void __launch_bounds__(256) strip_scan_kernel(const StripParams prm,
                 if (t < ka.T) {
                     const char* rows[4];
                     rows_at(r, rows);
-                    step_apply<K, Tin, Te, SR>(rows, ka, b, t, gc, valid, e, cache, s);
+                    step_apply<K, Tin, Te, SR>(rows, ka, b, t, gc, valid, e, cache, s, ob0 + s * os0,
+                                               ob1 + s * os1);
                 }
             }
-            if (last_rg) {
-#pragma unroll
-                for (int i = 0; i < VEC; ++i) carry[(cur ^ 1) * WS + c + i] = e[i];
-            }
+            if (last_rg) sts_planar<acc, VEC, LPR>(carry + (cur ^ 1) * WS, cl, e);
             // stage `slot` consumed, next carry visible; the whole CTA stops if
             // any thread's copy wait ran out
             if (__syncthreads_or(!ok)) {
@@ -316,9 +347,10 @@ __global__ void __launch_bounds__(256) strip_scan_kernel(const StripParams prm,
         // final state: E_{T-1} (forward) or the gradient w.r.t. e0 (reverse)
         if (ka.e_last != nullptr && rgl == 0 && warp == 0 && valid) {
             const int fin = (int)(prm.ntt & 1);
+            acc x[VEC];
+            lds_planar<acc, VEC, LPR>(carry + fin * WS, cl, x);
 #pragma unroll
-            for (int i = 0; i < VEC; ++i)
-                static_cast<acc*>(ka.e_last)[b * ka.hd + gc + i] = carry[fin * WS + c + i];
+            for (int i = 0; i < VEC; ++i) static_cast<acc*>(ka.e_last)[b * ka.hd + gc + i] = x[i];
         }
         __syncthreads();
     }
@@ -395,12 +427,21 @@ int strip_occupancy(int dev, int nstage) {
     return per_sm;
 }
 
+// Tuning overrides read once from the environment (0 = automatic):
+// ESA_STRIP_LPR (4/8/16/32 lanes per row) and ESA_STRIP_STAGES (2..8).
+inline int strip_env(const char* name) {
+    const char* v = getenv(name);
+    return v ? atoi(v) : 0;
+}
+
 // Picks the strip width (LPR) and pipeline depth for the call, or declines
 // (*taken = false) when the strips cannot fill the GPU (then the caller uses
-// the time-parallel lookback scan).  Preference order:
-//   1. every strip resident in one wave (no tail wave) with >= 3 stages;
-//   2. the same with 2 stages;
-//   3. the widest strips (longest DRAM rows, fewest CTAs) among those.
+// the time-parallel lookback scan).  Among configurations that keep every
+// strip resident in one wave (no tail wave), prefer
+//   1. at least two CTAs per SM (a lone 8-warp CTA cannot hide the per-tile
+//      barriers and shared-memory round trips);
+//   2. wider strips (longer DRAM rows, fewer CTAs);
+//   3. the most stages that fit (measured: 2 to 6 stages perform alike).
 template <Kind K, typename Tin, typename Te, int SR4, int SR8, int SR16, int SR32>
 int strip_launch_kind(const ScanCall& call, bool* taken) {
     *taken = false;
@@ -410,6 +451,8 @@ int strip_launch_kind(const ScanCall& call, bool* taken) {
     const int64_t T = call.a.T, nb = call.a.nb, hd = call.a.hd;
     using P = Policy<K, Tin, Te>;
     if (T < 16) return ESA_OK;
+    static const int force_lpr = strip_env("ESA_STRIP_LPR");
+    static const int force_ns = strip_env("ESA_STRIP_STAGES");
     auto strips = [&](int lpr) { return nb * ((hd + lpr * P::VEC - 1) / (lpr * P::VEC)); };
     auto occ = [&](int lpr, int ns) -> int {
         switch (lpr) {
@@ -420,25 +463,31 @@ int strip_launch_kind(const ScanCall& call, bool* taken) {
         }
     };
     int pick_lpr = 0, pick_ns = 0, pick_occ = 0;
-    for (int min_ns = 3; min_ns >= 2 && pick_lpr == 0; --min_ns) {
-        for (int lpr : {32, 16, 8, 4}) {
-            const int64_t n = strips(lpr);
-            if (n < (sms * 3) / 4) continue;  // too few strips to fill the GPU
-            for (int ns = 6; ns >= min_ns; --ns) {
-                const int o = occ(lpr, ns);
-                if (o > 0 && (int64_t)o * sms >= n) {
-                    pick_lpr = lpr;
-                    pick_ns = ns;
-                    pick_occ = o;
-                    break;
-                }
+    int64_t best = -1;
+    for (int lpr : {32, 16, 8, 4}) {
+        if (force_lpr && lpr != force_lpr) continue;
+        const int64_t n = strips(lpr);
+        if (n < (sms * 3) / 4) continue;  // too few strips to fill the GPU
+        const int64_t per_sm = (n + sms - 1) / sms;
+        for (int ns = 6; ns >= 2; --ns) {
+            if (force_ns && ns != force_ns) continue;
+            const int o = occ(lpr, ns);
+            if (o <= 0 || o < per_sm) continue;
+            // score: two or more CTAs per SM, then width
+            const int64_t score = (per_sm >= 2 ? 100 : 0) + lpr;
+            if (score > best) {
+                best = score;
+                pick_lpr = lpr;
+                pick_ns = ns;
+                pick_occ = o;
             }
-            if (pick_lpr) break;
+            break;  // the most stages that fit is the best for this width
         }
     }
     if (pick_lpr == 0) {
         // more strips than can be resident at once: 2 stages, persistent CTAs
         for (int lpr : {8, 16, 32, 4}) {
+            if (force_lpr && lpr != force_lpr) continue;
             const int o = occ(lpr, 2);
             if (strips(lpr) >= (sms * 3) / 4 && o > 0) {
                 pick_lpr = lpr;
