@@ -333,7 +333,7 @@ def run_ours(args) -> None:
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "mean_launch_ms": mean_launch_ms,
-                         "kernel": "tiled_scan_kernel<FwdPlain, half, half>",
+                         "kernel": "strip_scan_kernel<FwdPlain, __half, __half, LPR, SR> (strip width chosen per shape)",
                          "traffic": (traffic or {}).get("bytes_per_launch"),
                          "traffic_source": (traffic or {}).get("source")},
             "cpu_baseline": None,
@@ -354,15 +354,16 @@ def run_ours(args) -> None:
 
 
 def secondary(dev, stream, L, args) -> dict:
+    """Kernel-only GB/s of the other scan kinds and dtypes (algorithmic bytes):
+    forward fp32, bare reverse fp16/fp32, the fused gated forward/backward of a
+    [16, 2048, 768] fp16 layer, and a [74, 2048, 16, 64] fp16 forward whose
+    296 strips fill every SM evenly."""
     import torch
 
     from esa import _lib
 
-    nb, T, H, D = SHAPE
-    hd = H * D
-    N = nb * T * hd
-    out = {}
     sp = stream.cuda_stream
+    out = {}
 
     def timeit(fn, k=30):
         for _ in range(3):
@@ -378,35 +379,54 @@ def secondary(dev, stream, L, args) -> dict:
         return a.elapsed_time(b) / k
 
     g = torch.Generator(device=dev).manual_seed(99)
-    for name, dt, code, es in (("fwd_f32", torch.float32, _lib.DTYPE_F32, 4),):
-        A = torch.sigmoid(torch.randn(SHAPE, device=dev, generator=g) * 2 + 2).to(dt)
-        B = torch.randn(SHAPE, device=dev, generator=g).to(dt)
+    codes = {torch.float16: _lib.DTYPE_F16, torch.float32: _lib.DTYPE_F32}
+
+    def scans(shape, dt, tag):
+        nb, T, H, D = shape
+        hd = H * D
+        N = nb * T * hd
+        es = torch.empty((), dtype=dt).element_size()
+        code = codes[dt]
+        A = torch.sigmoid(torch.randn(shape, device=dev, generator=g) * 2 + 2).to(dt)
+        B = torch.randn(shape, device=dev, generator=g).to(dt)
         E = torch.empty_like(A)
-        for compass in (16, 32, 64):
-            wsb = L.esa_scan_workspace_bytes(nb, T, hd, code, compass)
-            w = torch.empty(wsb, dtype=torch.uint8, device=dev)
-            ms = timeit(lambda: L.esa_scan_fwd(A.data_ptr(), B.data_ptr(), E.data_ptr(), nb, T, hd,
-                                               code, compass, None, None, w.data_ptr(), wsb, sp))
-            out[f"{name}_c{compass}_GBps"] = 3 * N * es / (ms * 1e-3) / 1e9
-        del A, B, E
-    A = torch.sigmoid(torch.randn(SHAPE, device=dev, generator=g) * 2 + 2).half()
-    B = torch.randn(SHAPE, device=dev, generator=g).half()
-    E = torch.empty_like(A)
-    for compass in (32, 64):
-        wsb = L.esa_scan_workspace_bytes(nb, T, hd, _lib.DTYPE_F16, compass)
+        wsb = L.esa_scan_workspace_bytes(nb, T, hd, code, 16)
         w = torch.empty(wsb, dtype=torch.uint8, device=dev)
-        ms = timeit(lambda: L.esa_scan_fwd(A.data_ptr(), B.data_ptr(), E.data_ptr(), nb, T, hd,
-                                           _lib.DTYPE_F16, compass, None, None, w.data_ptr(), wsb, sp))
-        out[f"fwd_f16_c{compass}_GBps"] = 3 * N * 2 / (ms * 1e-3) / 1e9
-    dE = torch.randn(SHAPE, device=dev, generator=g).half()
-    dA = torch.empty_like(A)
-    dB = torch.empty_like(A)
-    wsb = L.esa_scan_workspace_bytes(nb, T, hd, _lib.DTYPE_F16, 16)
+        ms = timeit(lambda: L.esa_scan_fwd(A.data_ptr(), B.data_ptr(), E.data_ptr(), nb, T, hd, code, 16,
+                                           None, None, w.data_ptr(), wsb, sp))
+        out[f"fwd_{tag}_GBps"] = 3 * N * es / (ms * 1e-3) / 1e9
+        if tag.endswith("32x4096x16x64"):
+            dE = torch.randn(shape, device=dev, generator=g).to(dt)
+            dA = torch.empty_like(A)
+            dB = torch.empty_like(A)
+            ms = timeit(lambda: L.esa_scan_rev(A.data_ptr(), E.data_ptr(), dE.data_ptr(), dA.data_ptr(),
+                                               dB.data_ptr(), nb, T, hd, code, 16, None, None,
+                                               w.data_ptr(), wsb, sp))
+            out[f"rev_{tag}_GBps"] = 5 * N * es / (ms * 1e-3) / 1e9
+
+    scans(SHAPE, torch.float32, "f32_32x4096x16x64")
+    scans(SHAPE, torch.float16, "f16_32x4096x16x64")
+    scans((74, 2048, 16, 64), torch.float16, "f16_74x2048x16x64")
+    # fused gated scans of one ESA layer: qgv [16, 2048, 3*768] fp16
+    nb, T, C = 16, 2048, 768
+    qgv = torch.randn(nb, T, 3 * C, device=dev, generator=g).half()
+    gr, vr = qgv[..., C:2 * C], qgv[..., 2 * C:]
+    Eg = torch.empty(nb, T, C, device=dev, dtype=torch.float16)
+    dE = torch.randn(nb, T, C, device=dev, generator=g).half()
+    dg = torch.empty_like(Eg)
+    dv = torch.empty_like(Eg)
+    wsb = L.esa_scan_workspace_bytes(nb, T, C, _lib.DTYPE_F16, 16)
     w = torch.empty(wsb, dtype=torch.uint8, device=dev)
-    ms = timeit(lambda: L.esa_scan_rev(A.data_ptr(), E.data_ptr(), dE.data_ptr(), dA.data_ptr(),
-                                       dB.data_ptr(), nb, T, hd, _lib.DTYPE_F16, 16, None, None,
-                                       w.data_ptr(), wsb, sp))
-    out["rev_f16_c16_GBps"] = 5 * N * 2 / (ms * 1e-3) / 1e9
+    N = nb * T * C
+    ms = timeit(lambda: L.esa_gated_scan_fwd(gr.data_ptr(), vr.data_ptr(), 3 * C, _lib.DTYPE_F16,
+                                             Eg.data_ptr(), _lib.DTYPE_F16, nb, T, C, 0.8, 0.995, 1, 16,
+                                             None, None, w.data_ptr(), wsb, sp))
+    out["gated_fwd_f16_16x2048x768_GBps"] = 3 * N * 2 / (ms * 1e-3) / 1e9
+    ms = timeit(lambda: L.esa_gated_scan_bwd(gr.data_ptr(), vr.data_ptr(), 3 * C, _lib.DTYPE_F16,
+                                             Eg.data_ptr(), dE.data_ptr(), _lib.DTYPE_F16, dg.data_ptr(),
+                                             dv.data_ptr(), C, _lib.DTYPE_F16, nb, T, C, 0.8, 0.995, 1, 16,
+                                             None, None, w.data_ptr(), wsb, sp))
+    out["gated_bwd_f16_16x2048x768_GBps"] = 6 * N * 2 / (ms * 1e-3) / 1e9
     return out
 
 
