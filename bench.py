@@ -430,17 +430,232 @@ def secondary(dev, stream, L, args) -> dict:
     return out
 
 
+# ---------------------------------------------------------------------------
+# Model-level workloads (not the headline line): ESAModel training step
+# (config: 12 layers, embd 768, head 12, block 2048, vocab 32000, batch 16 per
+# GPU, fp16 autocast + GradScaler + AdamW, DDP across ranks), ESAModel decode
+# (24 layers, embd 1024, head 16, vocab 32000, 512-token prompt with
+# thunder_16 prefill, 256 greedy Lightning tokens, batch 1 and 64) and the
+# single ESA layer (embd 128, head 4, [16, 1024, 128], fp32, forward +
+# backward of sum(y)).  Random-init weights, synthetic tokens.
+# ---------------------------------------------------------------------------
+def _bf16_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d.get("bf16_tflops_sustained", d.get("bf16_tflops"))), "measured sustained"
+    return 1400.0, "fallback"
+
+
+def run_train(args) -> None:
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from esa import ESAModel, ESAModelConfig, ops
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    torch.manual_seed(1234)
+    cfg = ESAModelConfig(vocab_size=32000, block=2048, n_layer=12, head=12, embd=768,
+                         backend="thunder", precision="fp16", dropout=0.0, bias=True,
+                         tie_embeddings=True, training_compile=bool(args.compile))
+    model = ESAModel(cfg, device=f"cuda:{local}")
+    model.train()
+    n_params = sum(p.numel() for p in model.parameters())
+    net = model
+    if ws > 1:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local],
+                                                        gradient_as_bucket_view=True)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, fused=True)
+    scaler = torch.amp.GradScaler("cuda")
+    B, T = 16, 2048
+    g = torch.Generator().manual_seed(4321 + rank)
+    host_ids = torch.randint(0, 32000, (B, T + 1), generator=g).pin_memory()
+    ids = torch.empty_like(host_ids, device=dev)
+    host_loss = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def step():
+        ids.copy_(host_ids, non_blocking=True)
+        with torch.autocast("cuda", dtype=torch.float16):
+            _, loss = net(ids[:, :-1], ids[:, 1:])
+        scaler.scale(loss).backward()
+        scaler.step(opt)
+        scaler.update()
+        opt.zero_grad(set_to_none=True)
+        host_loss.copy_(loss.detach().float(), non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    if ws > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    stream = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    clk = clocks.stop()
+    ops.check_device_status(dev)
+    tok = ws * B * T * args.steps / (ms * 1e-3)
+    peak, kind = _bf16_peak()
+    flops_per_token = 6 * n_params
+    if rank == 0:
+        line = {
+            "metric": "esamodel_train_tokens_per_s", "value": tok, "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic tokens, random init",
+            "config": {"workload": "ESAModel train step 12L/768/12h, vocab 32000, block 2048, batch 16 "
+                                   "per GPU, fp16 autocast, AdamW, " + ("DDP" if ws > 1 else "1 GPU"),
+                       "compile": bool(args.compile), "params": n_params, "global_batch": B * ws,
+                       "seq_len": T, "parallelism": f"dp{ws}", "final_loss": float(host_loss)},
+            "roofline": {"bound": "tensor", "achieved": tok * flops_per_token / 1e12, "peak": peak,
+                         "unit": "TFLOP/s", "frac": tok * flops_per_token / 1e12 / peak,
+                         "peak_kind": kind, "flops_per_token": flops_per_token},
+            "e2e": {"value": tok, "unit": "tokens/s", "h2d_bytes_per_step": host_ids.numel() * 8,
+                    "d2h_bytes_per_step": 4},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
+
+
+def run_decode(args) -> None:
+    import torch
+
+    from esa import ESAModel, ESAModelConfig, ops
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    torch.manual_seed(1234)
+    prec = args.precision
+    cfg = ESAModelConfig(vocab_size=32000, n_layer=24, embd=1024, head=16, block=1024, dropout=0.0,
+                         precision=prec)
+    model = ESAModel(cfg, device=f"cuda:{local}").eval()
+    if prec == "fp16":
+        model = model.half()
+    n_params = sum(p.numel() for p in model.parameters())
+    wbytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    results = {}
+    for batch in (1, 64):
+        g = torch.Generator().manual_seed(77 + batch)
+        ids = torch.randint(0, 32000, (batch, 512), generator=g).to(dev)
+        for _ in range(max(1, args.warmup)):
+            model.generate(input_ids=ids, seek=16, prefill="thunder_16", temperature=0.0,
+                           compile=False, decode_graph=True)
+        res = model.generate(input_ids=ids, seek=256, prefill="thunder_16", temperature=0.0,
+                             compile=False, decode_graph=True, stats=True)
+        st = res.stats
+        results[f"batch{batch}"] = {
+            "prefill_tok_s": batch * st.prefill_tokens / st.prefill_seconds,
+            "decode_tok_s": batch * st.decode_tok_s,
+            "decode_ms_per_token": 1e3 * st.decode_seconds / max(1, st.decode_steps),
+            "weight_GBps": wbytes * st.decode_tok_s / 1e9,
+        }
+    ops.check_device_status(dev)
+    peak, pk = _peaks()
+    b1 = results["batch1"]
+    if rank == 0:
+        line = {
+            "metric": "esamodel_decode_tokens_per_s", "value": b1["decode_tok_s"], "unit": "tokens/s",
+            "n_gpus": 1, "steps": 256, "warmup": args.warmup, "ms_per_step": b1["decode_ms_per_token"],
+            "higher_is_better": True, "scaling": "replicas", "vs_baseline": None,
+            "dtype": "f16" if prec == "fp16" else "f32", "data": "synthetic prompt, random init",
+            "config": {"workload": "ESAModel 24L/1024/16h vocab 32000: 512-token thunder_16 prefill + "
+                                   "256 greedy ESA-Lightning tokens (CUDA-graph decode)",
+                       "precision": prec, "params": n_params, "weight_bytes": wbytes, **results},
+            "roofline": {"bound": "hbm", "achieved": b1["weight_GBps"], "peak": peak, "unit": "GB/s",
+                         "frac": b1["weight_GBps"] / peak, "peak_kind": pk,
+                         "note": "batch-1 decode reads every weight once per token"},
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_layer(args) -> None:
+    import torch
+
+    from esa import ESA, ops
+
+    torch.manual_seed(1234)
+    dev = torch.device("cuda", 0)
+    lay = ESA(embd=128, head=4, batch=16, block=1024, backend="thunder", precision="fp32", dropout=0.0,
+              device=dev)
+    x = torch.randn(16, 1024, 128, generator=torch.Generator().manual_seed(1234)).to(dev)
+
+    def step():
+        xi = x.detach().requires_grad_(True)
+        lay(xi).sum().backward()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    ops.check_device_status(dev)
+    line = {"metric": "esa_layer_fwd_bwd_ms", "value": ms, "unit": "ms", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "ESA(embd=128, head=4, thunder, fp32) forward + backward of sum(y), "
+                                   "x [16,1024,128]"}}
+    if not args.no_cpu:
+        import torch as _t
+        from oracle import oracle
+        _t.set_num_threads(os.cpu_count() or 1)
+        xc = x.cpu().double().requires_grad_(True)
+        qw = lay.layer.qgv.weight.detach().cpu().double().requires_grad_(True)
+        ow = lay.layer.out_proj.weight.detach().cpu().double().requires_grad_(True)
+        t0 = time.perf_counter()
+        oracle.pulse_layer_forward(xc, qw, ow, head=4).sum().backward()
+        line["cpu_baseline"] = {"value": (time.perf_counter() - t0) * 1e3, "unit": "ms",
+                                "cores": os.cpu_count() or 1, "kind": "port",
+                                "sample": "fp64 layer restatement with the C oracle scan, one step"}
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["scan", "train", "decode", "layer"], default="scan",
+                    help="scan (default, the headline line) or a model-level workload")
+    ap.add_argument("--compile", action="store_true", help="train: torch.compile the forward")
+    ap.add_argument("--precision", default="fp16", choices=["fp16", "fp32"], help="decode precision")
     ap.add_argument("--quick", action="store_true", help="skip the secondary figures")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "train":
+        run_train(args)
+    elif args.workload == "decode":
+        run_decode(args)
+    elif args.workload == "layer":
+        run_layer(args)
     else:
         run_ours(args)
 
