@@ -30,7 +30,10 @@ inline int dtype_size(int dtype) {
     }
 }
 
-enum class Kind { FwdPlain, FwdGated, RevPlain, RevGated };
+// FwdSummary: the forward recurrence over [0, T) reduced to its per-channel
+// end state and product of A (no per-step outputs): the summary of a time
+// slice, for composing slices held by different GPUs.
+enum class Kind { FwdPlain, FwdGated, RevPlain, RevGated, FwdSummary };
 
 // A row-strided view: element (row, c) at p + (row * rs + c) * elem_size,
 // row = b * T + t.
@@ -50,6 +53,7 @@ struct KArgs {
     int64_t nb, T, hd;
     const void* e0;    // acc [nb*hd] or null
     void* e_last;      // fwd: E_{T-1}; rev: gradient w.r.t. e0 (acc [nb*hd]) or null
+    void* prod_out;    // FwdSummary: product of A over [0, T) (acc [nb*hd])
     double gmin, span; // gate_min and gate_max - gate_min
     int round_ab;
     unsigned* status;  // device status word
@@ -90,6 +94,8 @@ int gated_scan_bwd(const void* g, const void* v, int64_t rrs, int raw_dtype, con
                    int64_t nb, int64_t T, int64_t hd, double gmin, double gmax, int round_ab,
                    int compass, const void* e0, void* de0, void* ws, size_t ws_bytes,
                    cudaStream_t s);
+int scan_summary(const void* A, const void* B, int64_t nb, int64_t T, int64_t hd, int dtype,
+                 const void* e0, void* e_last, void* prod, cudaStream_t s);
 size_t scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int compass);
 int lightning_step(const void* qgv, int64_t qrs, int qdt, const void* state, void* new_state,
                    int sdt, void* z, int zdt, int64_t nb, int64_t C, double gmin, double gmax,

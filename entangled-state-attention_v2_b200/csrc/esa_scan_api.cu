@@ -20,6 +20,7 @@ int strip_fwd_plain(const ScanCall& c, bool* taken);
 int strip_rev_plain(const ScanCall& c, bool* taken);
 int strip_fwd_gated(const ScanCall& c, bool* taken);
 int strip_rev_gated(const ScanCall& c, bool* taken);
+int strip_fwd_summary(const ScanCall& c, bool* taken);
 
 int strip_scan_launch(const ScanCall& c, bool* taken) {
     switch (c.kind) {
@@ -27,6 +28,7 @@ int strip_scan_launch(const ScanCall& c, bool* taken) {
         case Kind::RevPlain: return strip_rev_plain(c, taken);
         case Kind::FwdGated: return strip_fwd_gated(c, taken);
         case Kind::RevGated: return strip_rev_gated(c, taken);
+        case Kind::FwdSummary: return strip_fwd_summary(c, taken);
     }
     *taken = false;
     return ESA_OK;
@@ -102,7 +104,16 @@ __global__ void sequential_scan_kernel(const KArgs prm) {
         *p = Elem<T>::from_acc(static_cast<typename Elem<T>::acc>(val));
     };
     const acc e0v = prm.e0 ? static_cast<const acc*>(prm.e0)[ch] : acc(0);
-    if constexpr (!P::REV) {
+    if constexpr (K == Kind::FwdSummary) {
+        acc e = e0v, pr = acc(1);
+        for (int64_t t = 0; t < prm.T; ++t) {
+            const acc a = ld(0, t, Tin{});
+            e = a * e + ld(1, t, Tin{});
+            pr = pr * a;
+        }
+        if (prm.e_last) static_cast<acc*>(prm.e_last)[ch] = e;
+        if (prm.prod_out) static_cast<acc*>(prm.prod_out)[ch] = pr;
+    } else if constexpr (!P::REV) {
         acc e = e0v;
         for (int64_t t = 0; t < prm.T; ++t) {
             acc a, bb;
@@ -174,6 +185,9 @@ int sequential_scan_launch(const ScanCall& c) {
                 case Kind::RevPlain:
                     if constexpr (std::is_same<Tin, Te>::value) return seq_typed<Kind::RevPlain, Tin, Te>(c);
                     break;
+                case Kind::FwdSummary:
+                    if constexpr (std::is_same<Tin, Te>::value) return seq_typed<Kind::FwdSummary, Tin, Te>(c);
+                    break;
                 case Kind::FwdGated: return seq_typed<Kind::FwdGated, Tin, Te>(c);
                 case Kind::RevGated: return seq_typed<Kind::RevGated, Tin, Te>(c);
             }
@@ -211,6 +225,8 @@ int run(ScanCall& c) {
     bool taken = false;
     const int rc = strip_scan_launch(c, &taken);
     if (rc != ESA_OK || taken) return rc;
+    // the summary has no time-parallel form: one thread per channel
+    if (c.kind == Kind::FwdSummary) return sequential_scan_launch(c);
     return lookback_scan_launch(c);
 }
 
@@ -242,6 +258,30 @@ int scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64
     c.ws_bytes = ws_bytes;
     c.stream = s;
     c.bulk_ok = rows_aligned(A, hd, hd, es) && rows_aligned(B, hd, hd, es) && rows_aligned(E, hd, hd, es);
+    return run(c);
+}
+
+int scan_summary(const void* A, const void* B, int64_t nb, int64_t T, int64_t hd, int dtype,
+                 const void* e0, void* e_last, void* prod, cudaStream_t s) {
+    if (int rc = check_dims(nb, T, hd, 16)) return rc;
+    const int es = dtype_size(dtype);
+    if (es == 0) return set_error(ESA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code " + std::to_string(dtype));
+    if (nb * T * hd > 0 && (!A || !B)) return set_error(ESA_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (nb * hd > 0 && (!e_last || !prod)) return set_error(ESA_ERR_INVALID_ARGUMENT, "null output pointer");
+    ScanCall c{};
+    c.kind = Kind::FwdSummary;
+    c.tin = c.te = dtype;
+    c.a.in[0] = {static_cast<const char*>(A), hd};
+    c.a.in[1] = {static_cast<const char*>(B), hd};
+    c.a.nb = nb;
+    c.a.T = T;
+    c.a.hd = hd;
+    c.a.e0 = e0;
+    c.a.e_last = e_last;
+    c.a.prod_out = prod;
+    c.compass = 16;
+    c.stream = s;
+    c.bulk_ok = rows_aligned(A, hd, hd, es) && rows_aligned(B, hd, hd, es);
     return run(c);
 }
 

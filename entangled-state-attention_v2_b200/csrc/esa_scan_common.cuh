@@ -220,7 +220,7 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
                                           typename P::template Cache<S>& cache, int s) {
     using acc = typename P::acc;
     constexpr int VEC = P::VEC;
-    if constexpr (K == Kind::FwdPlain) {
+    if constexpr (K == Kind::FwdPlain || K == Kind::FwdSummary) {
         load_smem<Tin, VEC>(rows[0], a);
         load_smem<Tin, VEC>(rows[1], b);
 #pragma unroll

@@ -551,6 +551,7 @@ int lookback_scan_launch(const ScanCall& c) {
                     break;
                 case Kind::FwdGated: return launch_typed<Kind::FwdGated, Tin, Te>(c);
                 case Kind::RevGated: return launch_typed<Kind::RevGated, Tin, Te>(c);
+                case Kind::FwdSummary: break;
             }
             return set_error(ESA_ERR_UNSUPPORTED_DTYPE, "plain scans need one dtype");
         });

@@ -177,6 +177,9 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
         auto tile_t0 = [&](int64_t j) -> int64_t {
             return (P::REV ? (prm.ntt - 1 - j) : j) * (int64_t)LT;
         };
+        acc prod_run[VEC];  // FwdSummary: product of A so far (last row group's lanes)
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) prod_run[i] = acc(1);
         // initial carry: e0 (forward) or zero (reverse: nothing after T)
         if (rgl == 0 && warp == 0) {
             acc x[VEC];
@@ -307,10 +310,19 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
                 vfma(eb, aw, eb, bw);
                 vmul(ea, aw, ea);
             }
-            // ---- phase 3: incoming state, re-run, outputs ------------------
             acc e[VEC];
             lds_planar<acc, VEC, LPR>(carry + cur * WS, cl, e);
             vfma(e, ea, e, eb);  // through the warps before this one
+            if constexpr (K == Kind::FwdSummary) {
+                // no per-step outputs: the last row group's warp-inclusive pair
+                // carries the state to the tile end; the product of A follows
+                if (last_rg) {
+                    vfma(e, pa, e, pb);
+                    vmul(prod_run, prod_run, ea);
+                    vmul(prod_run, prod_run, pa);
+                }
+            } else {
+            // ---- phase 3: incoming state, re-run, outputs ------------------
             vfma(e, xa, e, xb);  // through the row groups before this one
             // output addresses of this row group's first step; one row stride per step
             const int64_t orow0 = b * ka.T + t0 + rg * SR;
@@ -329,6 +341,7 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
                                                ob1 + s * os1);
                 }
             }
+            }
             if (last_rg) sts_planar<acc, VEC, LPR>(carry + (cur ^ 1) * WS, cl, e);
             // stage `slot` consumed, next carry visible; the whole CTA stops if
             // any thread's copy wait ran out
@@ -344,6 +357,12 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
             }
         }
         if (aborted) break;
+        if constexpr (K == Kind::FwdSummary) {
+            if (last_rg && valid) {
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) static_cast<acc*>(ka.prod_out)[b * ka.hd + gc + i] = prod_run[i];
+            }
+        }
         // final state: E_{T-1} (forward) or the gradient w.r.t. e0 (reverse)
         if (ka.e_last != nullptr && rgl == 0 && warp == 0 && valid) {
             const int fin = (int)(prm.ntt & 1);

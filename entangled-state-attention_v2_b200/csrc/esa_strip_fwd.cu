@@ -11,4 +11,11 @@ int strip_fwd_plain(const ScanCall& c, bool* taken) {
     });
 }
 
+int strip_fwd_summary(const ScanCall& c, bool* taken) {
+    return dispatch_dtype(c.te, [&](auto tag) -> int {
+        using T = decltype(tag);
+        return strip_launch_kind<Kind::FwdSummary, T, T, 1, 2, 4, 4>(c, taken);
+    });
+}
+
 }  // namespace esa

@@ -177,6 +177,35 @@ def _scan_bwd(ctx, dE, de_last):
 torch.library.register_autograd("esa_b200::scan", _scan_bwd, setup_context=_scan_setup)
 
 
+@torch.library.custom_op("esa_b200::scan_summary", mutates_args=())
+def scan_summary(A: Tensor, B: Tensor, e0: Optional[Tensor]) -> tuple[Tensor, Tensor]:
+    """Per-channel (E_{T-1}, prod_t A_t) of a time slice, [B, H*D] in the acc
+    dtype; reads A and B once and writes no per-step output."""
+    _require_cuda("esa scan summary", A, B, e0)
+    nb, T, H, D = A.shape
+    hd = H * D
+    A = A.contiguous()
+    B = B.to(A.dtype).contiguous()
+    acc = acc_dtype(A.dtype)
+    e0c = _state_arg(e0, nb, hd, acc)
+    if T == 0 or nb * hd == 0:
+        e_last = e0c.clone() if e0c is not None else A.new_zeros(nb, hd, dtype=acc)
+        return e_last, A.new_ones(nb, hd, dtype=acc)
+    e_last = torch.empty(nb, hd, dtype=acc, device=A.device)
+    prod = torch.empty(nb, hd, dtype=acc, device=A.device)
+    rc = _lib.lib().esa_scan_summary(A.data_ptr(), B.data_ptr(), nb, T, hd, dtype_code(A.dtype),
+                                     _ptr(e0c), e_last.data_ptr(), prod.data_ptr(), _stream(A))
+    _lib.check(rc, "esa_scan_summary")
+    return e_last, prod
+
+
+@scan_summary.register_fake
+def _(A, B, e0):
+    nb, T, H, D = A.shape
+    acc = acc_dtype(A.dtype)
+    return A.new_empty(nb, H * D, dtype=acc), A.new_empty(nb, H * D, dtype=acc)
+
+
 # --------------------------------------------------------------------------
 # Gated scan: gate prologue fused into the forward, gate epilogue fused into
 # the reverse scan (ThunderESA.forward, esa_prefill)

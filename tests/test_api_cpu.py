@@ -23,7 +23,7 @@ def test_header_declares_the_abi():
     assert set(syms) == {
         "esa_abi_version", "esa_last_error", "esa_device_status", "esa_scan_workspace_bytes",
         "esa_scan_fwd", "esa_scan_rev", "esa_gated_scan_fwd", "esa_gated_scan_bwd",
-        "esa_lightning_step", "esa_scan_fwd_noalloc"}
+        "esa_lightning_step", "esa_scan_fwd_noalloc", "esa_scan_summary"}
 
 
 def test_library_loads_and_exports_every_declared_symbol():

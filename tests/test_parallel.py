@@ -1,0 +1,166 @@
+"""Sequence-parallel scan: the carry exchange and composition.
+
+CPU part (gloo, world size 2 and 3): every rank summarises its time slice
+with the fp64 oracle, the summaries are all-gathered over gloo, and each rank
+composes its incoming state with esa.parallel.compose_carries; the states
+must equal the oracle's full-sequence state at the slice boundaries.
+GPU part: the same slices on one GPU through esa_scan_summary + the seeded
+scan, and (with two or more GPUs) the real NCCL path.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import oracle
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _slices(world, T=120, shape=(2, 3, 8), seed=0):
+    rng = np.random.default_rng(seed)
+    nb, H, D = shape
+    A = 1 / (1 + np.exp(-(rng.normal(size=(nb, T, H, D)) + 3)))
+    B = rng.normal(scale=0.5, size=(nb, T, H, D))
+    cuts = np.linspace(0, T, world + 1).astype(int)
+    return A, B, cuts
+
+
+def _gloo_worker(rank, world, port, result_q):
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root / "entangled-state-attention_v2_b200"))
+    sys.path.insert(0, str(root))
+    from esa.parallel import compose_carries
+    from oracle import oracle as orc
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        A, B, cuts = _slices(world)
+        a, b = A[:, cuts[rank]:cuts[rank + 1]], B[:, cuts[rank]:cuts[rank + 1]]
+        nb, _, H, D = a.shape
+        E = orc.scan_fwd(a, b)
+        e_end = torch.from_numpy(E[:, -1].reshape(nb, H * D))
+        prod = torch.from_numpy(np.prod(a, axis=1).reshape(nb, H * D))
+        mine = torch.stack([e_end, prod])
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine)
+        carry = compose_carries(gathered, rank)
+        result_q.put((rank, carry.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_carry_exchange_over_gloo(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    A, B, cuts = _slices(world)
+    full = oracle.scan_fwd(A, B)
+    nb, T, H, D = A.shape
+    for r in range(world):
+        expect = np.zeros((nb, H * D)) if r == 0 else full[:, cuts[r] - 1].reshape(nb, H * D)
+        np.testing.assert_allclose(got[r], expect, rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 2e-3)])
+def test_summary_and_sliced_scan_on_one_gpu(dtype, tol):
+    from esa import ops
+    from esa.parallel import compose_carries
+    torch.manual_seed(0)
+    nb, T, H, D = 4, 4096, 32, 64
+    A = torch.sigmoid(torch.randn(nb, T, H, D, device="cuda") + 3).to(dtype)
+    B = (torch.randn(nb, T, H, D, device="cuda") * 0.5).to(dtype)
+    world = 4
+    cuts = [i * T // world for i in range(world + 1)]
+    summaries = []
+    for r in range(world):
+        e_end, prod = ops.scan_summary(A[:, cuts[r]:cuts[r + 1]], B[:, cuts[r]:cuts[r + 1]], None)
+        summaries.append(torch.stack([e_end, prod]))
+    # summary of a slice against the oracle
+    a0 = A[:, :cuts[1]].double().cpu()
+    b0 = B[:, :cuts[1]].double().cpu()
+    ref0 = oracle.scan_fwd(a0, b0)
+    e_ref = ref0[:, -1].reshape(nb, H * D)
+    p_ref = np.prod(a0.numpy(), axis=1).reshape(nb, H * D)
+    np.testing.assert_allclose(summaries[0][0].double().cpu().numpy(), e_ref, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(summaries[0][1].double().cpu().numpy(), p_ref, rtol=1e-4, atol=1e-30)
+    parts = []
+    for r in range(world):
+        carry = compose_carries(summaries, r)
+        E, _ = ops.scan(A[:, cuts[r]:cuts[r + 1]], B[:, cuts[r]:cuts[r + 1]], carry, 16)
+        parts.append(E)
+    got = torch.cat(parts, dim=1).double().cpu().numpy()
+    ref = oracle.scan_fwd(A.double().cpu(), B.double().cpu())
+    err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert err < tol, err
+
+
+def _nccl_worker(rank, world, port, q):
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root / "entangled-state-attention_v2_b200"))
+    import datetime
+    from esa.parallel import sequence_parallel_scan
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        g = torch.Generator().manual_seed(1)
+        nb, T, H, D = 2, 2048, 8, 64
+        A = torch.sigmoid(torch.randn(nb, T, H, D, generator=g) + 3)
+        B = torch.randn(nb, T, H, D, generator=g) * 0.5
+        cuts = [i * T // world for i in range(world + 1)]
+        sl = slice(cuts[rank], cuts[rank + 1])
+        E = sequence_parallel_scan(A[:, sl].cuda(), B[:, sl].cuda())
+        torch.cuda.synchronize()
+        q.put((rank, E.cpu().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_sequence_parallel_scan_nccl():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    g = torch.Generator().manual_seed(1)
+    nb, T, H, D = 2, 2048, 8, 64
+    A = torch.sigmoid(torch.randn(nb, T, H, D, generator=g) + 3)
+    B = torch.randn(nb, T, H, D, generator=g) * 0.5
+    ref = oracle.scan_fwd(A.double(), B.double())
+    full = np.concatenate([got[r] for r in range(world)], axis=1)
+    assert np.linalg.norm(full - ref) / np.linalg.norm(ref) < 1e-5
