@@ -66,6 +66,19 @@ ESA_EXPORT int esa_scan_fwd(const void* A, const void* B, void* E, int64_t nb, i
                     static_cast<cudaStream_t>(stream));
 }
 
+ESA_EXPORT size_t esa_scan_host_staging_bytes(int64_t nb, int64_t T, int64_t hd, int dtype, int compass) {
+    const int es = dtype_size(dtype);
+    if (es == 0 || nb < 0 || T < 0 || hd < 0 || compass <= 0) return 0;
+    return scan_host_staging_bytes(nb, T, hd, es, compass);
+}
+
+ESA_EXPORT int esa_scan_fwd_host(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd,
+                                 int dtype, int compass, void* staging, size_t staging_bytes, void* stream) {
+    clear_error();
+    return scan_fwd_host(A, B, E, nb, T, hd, dtype, compass, staging, staging_bytes,
+                         static_cast<cudaStream_t>(stream));
+}
+
 ESA_EXPORT int esa_scan_summary(const void* A, const void* B, int64_t nb, int64_t T, int64_t hd,
                                 int dtype, const void* e0, void* e_last, void* prod, void* stream) {
     clear_error();

@@ -44,6 +44,57 @@ def thunder_scan(A: torch.Tensor, B_write: torch.Tensor, compass: int = 16,
     return E
 
 
+def thunder_scan_host(A: torch.Tensor, B_write: torch.Tensor, compass: int = 16,
+                      c: int | None = None, *, out: torch.Tensor | None = None,
+                      device: torch.device | int | None = None) -> torch.Tensor:
+    """thunder_scan of CPU tensors, computed on a GPU: the result is a CPU tensor.
+
+    A and B_write stay in host memory; the library streams them through the
+    device in chunks, overlapping the host-to-device copies, the scans and the
+    device-to-host copies (``esa_scan_fwd_host``).  Page-locked inputs and
+    ``out`` (``tensor.pin_memory()``) let the copies run asynchronously;
+    pageable memory works at a lower rate.  Returns when E is complete.  No
+    autograd (the reference's CPU thunder_scan is differentiable; use
+    thunder_scan on device tensors for training).
+    """
+    from .. import _lib
+
+    if c is not None:
+        compass = c
+    _check_scan_args(A, B_write)
+    _check_compass(compass)
+    if A.device.type != "cpu" or B_write.device.type != "cpu":
+        raise ValueError("thunder_scan_host takes CPU tensors; use thunder_scan for device tensors")
+    if not torch.cuda.is_available():
+        raise RuntimeError("thunder_scan_host needs a CUDA device (no CPU fallback)")
+    if A.dtype != B_write.dtype:
+        B_write = B_write.to(A.dtype)
+    A = A.contiguous()
+    B_write = B_write.contiguous()
+    if out is None:
+        out = torch.empty(A.shape, dtype=A.dtype, pin_memory=A.is_pinned())
+    elif out.shape != A.shape or out.dtype != A.dtype or not out.is_contiguous() or out.device.type != "cpu":
+        raise ValueError("out must be a contiguous CPU tensor of A's shape and dtype")
+    if device is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    else:
+        dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+    nb, T, H, D = A.shape
+    code = ops.dtype_code(A.dtype)
+    L = _lib.lib()
+    nbytes = int(L.esa_scan_host_staging_bytes(nb, T, H * D, code, int(compass)))
+    with torch.cuda.device(dev):
+        staging = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        _lib.check(L.esa_scan_fwd_host(A.data_ptr(), B_write.data_ptr(), out.data_ptr(), nb, T, H * D,
+                                       code, int(compass), staging.data_ptr(), nbytes,
+                                       stream.cuda_stream), "esa_scan_fwd_host")
+        stream.synchronize()
+        ops.check_device_status(dev)
+        del staging
+    return out
+
+
 class ThunderESA(nn.Module):
     """Thunder backend layer: reference constructor (thunder.py:186-261)."""
 

@@ -102,6 +102,26 @@ int esa_scan_fwd(const void *A, const void *B, void *E, int64_t nb, int64_t T, i
 int esa_scan_fwd_noalloc(const void *A, const void *B, void *E, int64_t nb, int64_t T, int64_t hd,
                          int dtype, int compass, const void *e0, void *e_last, void *stream);
 
+/* Staging size (bytes) of esa_scan_fwd_host for this problem; 0 for invalid
+ * arguments.  Bounded (about 80 MB) whatever the problem size. */
+size_t esa_scan_host_staging_bytes(int64_t nb, int64_t T, int64_t hd, int dtype, int compass);
+
+/* esa_scan_fwd on HOST buffers: A, B and E are host pointers ([nb, T, hd] of
+ * `dtype`, page-locked for the copies to overlap; pageable memory works but
+ * serialises), `staging` a 256-byte aligned device buffer of at least
+ * esa_scan_host_staging_bytes().  The tensor moves through the device in
+ * chunks of about 8 MB per array (whole rows, or time pieces of one row
+ * chained through their end state): the host-to-device copy of one chunk, the
+ * scan of the previous one (on `stream`) and the device-to-host copy of the
+ * one before run concurrently on the two copy engines and the SMs.  Ordered
+ * after the work already on `stream`; work queued on `stream` afterwards (an
+ * event record, cudaStreamSynchronize) sees E complete.  The library's own two
+ * copy streams are created on the first call per device.  Replaces
+ * thunder_scan on CPU tensors (esa/backends/thunder.py:70-159), whose output
+ * is a CPU tensor. */
+int esa_scan_fwd_host(const void *A, const void *B, void *E, int64_t nb, int64_t T, int64_t hd,
+                      int dtype, int compass, void *staging, size_t staging_bytes, void *stream);
+
 /* Summary of a time slice: the per-channel end state E_{T-1} of the forward
  * recurrence (from e0, NULL: zero) and the product of A over [0, T), both in
  * the acc type, [nb, hd]; no per-step outputs (reads A and B once).  Two

@@ -23,7 +23,8 @@ def test_header_declares_the_abi():
     assert set(syms) == {
         "esa_abi_version", "esa_last_error", "esa_device_status", "esa_scan_workspace_bytes",
         "esa_scan_fwd", "esa_scan_rev", "esa_gated_scan_fwd", "esa_gated_scan_bwd",
-        "esa_lightning_step", "esa_scan_fwd_noalloc", "esa_scan_summary"}
+        "esa_lightning_step", "esa_scan_fwd_noalloc", "esa_scan_summary",
+        "esa_scan_host_staging_bytes", "esa_scan_fwd_host"}
 
 
 def test_library_loads_and_exports_every_declared_symbol():
@@ -44,6 +45,19 @@ def test_workspace_size_is_pure_host_arithmetic():
     assert n16 > 0 and n32 > 0
     assert L.esa_scan_workspace_bytes(32, 4096, 1024, 9, 16) == 0      # bad dtype
     assert L.esa_scan_workspace_bytes(32, 4096, 1024, _lib.DTYPE_F16, 0) == 0  # bad compass
+
+
+def test_host_staging_is_bounded():
+    from esa import _lib
+    L = _lib.lib()
+    small = L.esa_scan_host_staging_bytes(2, 64, 128, _lib.DTYPE_F16, 16)
+    big = L.esa_scan_host_staging_bytes(32, 4096, 1024, _lib.DTYPE_F16, 16)
+    huge = L.esa_scan_host_staging_bytes(4, 262144, 2048, _lib.DTYPE_BF16, 16)
+    assert 0 < small <= big
+    assert big < 128 << 20 and huge < 128 << 20
+    assert L.esa_scan_host_staging_bytes(2, 64, 128, 9, 16) == 0
+    rc = L.esa_scan_fwd_host(None, None, None, 1, 4, 8, _lib.DTYPE_F32, 16, None, 0, None)
+    assert rc == -1 and "null host pointer" in _lib.last_error()
 
 
 def test_abi_argument_errors_need_no_gpu():

@@ -232,3 +232,29 @@ def test_microbenchmark_size_properties(dtype):
         lhs = thunder_scan(A, B + B2)
         rhs = thunder_scan(A, B) + thunder_scan(A, B2)
         assert rel(lhs, rhs) < 1e-5
+
+
+@pytest.mark.parametrize("shape,dtype,pinned", [
+    ((6, 300, 4, 64), torch.float32, True),       # whole rows, several rows per chunk
+    ((2, 9000, 4, 128), torch.float32, True),     # 18 MB rows: time pieces chained by e_last
+    ((3, 40000, 2, 64), torch.bfloat16, True),    # bf16 time pieces with a ragged last piece
+    ((5, 77, 3, 16), torch.float64, False),       # pageable host memory
+])
+def test_host_pipelined_scan(shape, dtype, pinned):
+    """thunder_scan_host: CPU tensors in, CPU tensor out, chunks streamed
+    through the device; equals the oracle on the same inputs."""
+    from esa.backends.thunder import thunder_scan_host
+    g = torch.Generator().manual_seed(7)
+    A = torch.sigmoid(torch.randn(shape, generator=g, dtype=torch.float64) + 2.5).to(dtype)
+    B = (torch.randn(shape, generator=g, dtype=torch.float64) * 0.5).to(dtype)
+    if pinned:
+        A, B = A.pin_memory(), B.pin_memory()
+    E = thunder_scan_host(A, B, compass=16)
+    assert E.device.type == "cpu" and E.dtype == dtype and E.shape == A.shape
+    ref = oracle.scan_fwd(A.double(), B.double())
+    assert rel(E, ref) < TOL[dtype]
+    # into a caller's buffer (pageable): same result within the bar (the
+    # time-parallel kernel's association order may differ from call to call)
+    out = torch.empty_like(E)
+    assert thunder_scan_host(A, B, out=out) is out
+    assert rel(out, ref) < TOL[dtype]
