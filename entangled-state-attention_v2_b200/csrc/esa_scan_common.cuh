@@ -83,59 +83,27 @@ struct Policy {
 };
 
 // ---------------------------------------------------------------------------
-// Lane-vector arithmetic.  fp32 vectors use Blackwell's packed two-lane FP32
-// instructions (__ffma2_rn / __fmul2_rn / __fadd2_rn: one instruction per
-// channel pair, IEEE round-to-nearest per lane, the same results as scalar
-// fmaf/__fmul_rn/__fadd_rn); fp64 vectors use scalar instructions.
+// Lane-vector arithmetic, one scalar IEEE round-to-nearest instruction per
+// channel.  (Blackwell's packed FP32x2 forms measured slower in these kernels:
+// their register-pair operands cost more moves than the pairing saves.)
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ float fma_rn(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+__device__ __forceinline__ double fma_rn(double a, double b, double c) { return __fma_rn(a, b, c); }
 // d = a * b + c
-template <int N>
-__device__ __forceinline__ void vfma(float (&d)[N], const float (&a)[N], const float (&b)[N],
-                                     const float (&c)[N]) {
-    static_assert(N % 2 == 0, "pairs");
+template <typename A, int N>
+__device__ __forceinline__ void vfma(A (&d)[N], const A (&a)[N], const A (&b)[N], const A (&c)[N]) {
 #pragma unroll
-    for (int i = 0; i < N; i += 2) {
-        const float2 r = __ffma2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]),
-                                   make_float2(c[i], c[i + 1]));
-        d[i] = r.x;
-        d[i + 1] = r.y;
-    }
-}
-template <int N>
-__device__ __forceinline__ void vfma(double (&d)[N], const double (&a)[N], const double (&b)[N],
-                                     const double (&c)[N]) {
-#pragma unroll
-    for (int i = 0; i < N; ++i) d[i] = fma(a[i], b[i], c[i]);
+    for (int i = 0; i < N; ++i) d[i] = fma_rn(a[i], b[i], c[i]);
 }
 // d = a * b
-template <int N>
-__device__ __forceinline__ void vmul(float (&d)[N], const float (&a)[N], const float (&b)[N]) {
-    static_assert(N % 2 == 0, "pairs");
-#pragma unroll
-    for (int i = 0; i < N; i += 2) {
-        const float2 r = __fmul2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]));
-        d[i] = r.x;
-        d[i + 1] = r.y;
-    }
-}
-template <int N>
-__device__ __forceinline__ void vmul(double (&d)[N], const double (&a)[N], const double (&b)[N]) {
+template <typename A, int N>
+__device__ __forceinline__ void vmul(A (&d)[N], const A (&a)[N], const A (&b)[N]) {
 #pragma unroll
     for (int i = 0; i < N; ++i) d[i] = a[i] * b[i];
 }
 // d = a + b
-template <int N>
-__device__ __forceinline__ void vadd(float (&d)[N], const float (&a)[N], const float (&b)[N]) {
-    static_assert(N % 2 == 0, "pairs");
-#pragma unroll
-    for (int i = 0; i < N; i += 2) {
-        const float2 r = __fadd2_rn(make_float2(a[i], a[i + 1]), make_float2(b[i], b[i + 1]));
-        d[i] = r.x;
-        d[i + 1] = r.y;
-    }
-}
-template <int N>
-__device__ __forceinline__ void vadd(double (&d)[N], const double (&a)[N], const double (&b)[N]) {
+template <typename A, int N>
+__device__ __forceinline__ void vadd(A (&d)[N], const A (&a)[N], const A (&b)[N]) {
 #pragma unroll
     for (int i = 0; i < N; ++i) d[i] = a[i] + b[i];
 }
@@ -191,18 +159,38 @@ __device__ __forceinline__ void sts_vec(A* p, const A (&in)[N]) {
     *reinterpret_cast<VecN<A, N>*>(p) = v;
 }
 
+// One vector store of W 32-bit words (W = 1, 2, 4): a single st.global.v4 /
+// v2 / b32 (a struct copy of __half2 elements would be split per element).
+template <int W>
+__device__ __forceinline__ void store_words(char* p, const uint32_t (&w)[W]) {
+    if constexpr (W == 4) {
+        *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else if constexpr (W == 2) {
+        *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < W; ++i) reinterpret_cast<uint32_t*>(p)[i] = w[i];
+    }
+}
+
 template <typename T, int N, typename A>
 __device__ __forceinline__ void store_global(char* p, const A (&in)[N]) {
     if constexpr (std::is_same<T, __half>::value && std::is_same<A, float>::value && N % 2 == 0) {
-        VecN<__half2, N / 2> v;
+        uint32_t w[N / 2];
 #pragma unroll
-        for (int i = 0; i < N / 2; ++i) v.v[i] = __floats2half2_rn(in[2 * i], in[2 * i + 1]);
-        *reinterpret_cast<VecN<__half2, N / 2>*>(p) = v;
+        for (int i = 0; i < N / 2; ++i) {
+            const __half2 h = __floats2half2_rn(in[2 * i], in[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        store_words<N / 2>(p, w);
     } else if constexpr (std::is_same<T, __nv_bfloat16>::value && std::is_same<A, float>::value && N % 2 == 0) {
-        VecN<__nv_bfloat162, N / 2> v;
+        uint32_t w[N / 2];
 #pragma unroll
-        for (int i = 0; i < N / 2; ++i) v.v[i] = __floats2bfloat162_rn(in[2 * i], in[2 * i + 1]);
-        *reinterpret_cast<VecN<__nv_bfloat162, N / 2>*>(p) = v;
+        for (int i = 0; i < N / 2; ++i) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(in[2 * i], in[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        store_words<N / 2>(p, w);
     } else {
         VecN<T, N> v;
 #pragma unroll

@@ -35,6 +35,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <type_traits>
 
 #include "esa_scan_common.cuh"
 
@@ -46,6 +47,7 @@ struct StripParams {
     int64_t nitems;  // nb * spr
     int64_t ntt;     // tiles along T = ceil(T / LT)
     int nstage;
+    int prefetch;    // tiles prefetched into L2 ahead of the shared-memory ring
 };
 
 template <Kind K, typename Tin, typename Te, int LPR_, int SR_>
@@ -82,6 +84,22 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
         ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;"
         :: "r"(d), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(b), "l"(policy)
         : "memory");
+}
+
+// L2 prefetch of one tile (no shared memory, no completion): raises the
+// bytes in flight from DRAM beyond what the shared-memory ring holds.
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, int y, int z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];"
+                 :: "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z) : "memory");
+}
+
+template <class Cfg>
+__device__ __forceinline__ void strip_prefetch(const StripParams& prm, const CUtensorMap* const (&maps)[4],
+                                               int64_t b, int64_t strip, int64_t t0) {
+    using P = typename Cfg::P;
+#pragma unroll
+    for (int a = 0; a < P::NIN; ++a)
+        tma_prefetch_3d(maps[a], (int)(strip * Cfg::WS), (int)(t0 + P::shift(a)), (int)b);
 }
 
 template <class Cfg>
@@ -141,7 +159,10 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
     const int nstage = prm.nstage;
 
     extern __shared__ __align__(128) char smem_raw[];
-    char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    // 128-byte aligned base, derived from the shared array itself so that the
+    // compiler keeps every pointer below in the shared window (LDS/STS, not
+    // generic loads)
+    char* smem = smem_raw + ((128u - (static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw)) & 127u)) & 127u);
     // per-warp tile aggregates [NW][WS]
     acc* wagg_a = reinterpret_cast<acc*>(smem + (size_t)nstage * Cfg::stage_bytes());
     acc* wagg_b = wagg_a + NW * WS;
@@ -168,6 +189,8 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
 
     uint64_t used = 0;    // tiles consumed by this CTA so far (stage = used % nstage)
     uint64_t issued = 0;  // tiles whose copies this CTA has issued
+    int slot = 0;         // ring stage of the next tile to consume (= used % nstage)
+    unsigned parity = 0;  // its mbarrier phase parity (= (used / nstage) & 1)
     bool aborted = false;
     for (int64_t item = blockIdx.x; item < prm.nitems && !aborted; item += gridDim.x) {
         const int64_t b = item / prm.spr;
@@ -192,18 +215,18 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
         // prologue: fill the ring
         const int npro = (int)(prm.ntt < nstage ? prm.ntt : nstage);
         if (threadIdx.x == 0) {
-            for (int s = 0; s < npro; ++s) {
-                const int slot = (int)((used + s) % nstage);
-                strip_issue<Cfg>(prm, maps, smem + (size_t)slot * Cfg::stage_bytes(), &bars[slot], b,
+            for (int s = npro; s < npro + prm.prefetch && s < prm.ntt; ++s)
+                strip_prefetch<Cfg>(prm, maps, b, strip, tile_t0(s));
+            for (int s = 0, sl = slot; s < npro; ++s) {
+                strip_issue<Cfg>(prm, maps, smem + (size_t)sl * Cfg::stage_bytes(), &bars[sl], b,
                                  strip, tile_t0(s), policy);
+                if (++sl == nstage) sl = 0;
             }
         }
         issued += npro;
         __syncthreads();
 
         for (int64_t j = 0; j < prm.ntt; ++j, ++used) {
-            const int slot = (int)(used % nstage);
-            const unsigned parity = (unsigned)((used / nstage) & 1);
             const int cur = (int)(j & 1);
             const int64_t t0 = tile_t0(j);
             const bool ok = mbar_wait_bounded(&bars[slot], parity, ka.status);
@@ -223,19 +246,29 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
                 pa[i] = acc(1);
                 pb[i] = acc(0);
             }
+            // every step of this row group inside [0, T) (all but the last tile):
+            // the step loops run without per-step bounds checks
+            const bool rg_full = t0 + (rg + 1) * SR <= ka.T;
+            auto phase1 = [&](auto full_tag) {
+                constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll
-            for (int ss = 0; ss < SR; ++ss) {
-                const int s = P::REV ? (SR - 1 - ss) : ss;
-                const int r = rg * SR + s;
-                if (t0 + r < ka.T) {
-                    const char* rows[4];
-                    rows_at(r, rows);
-                    acc a[VEC], bb[VEC];
-                    step_coef<K, Tin, Te, SR>(rows, ka, a, bb, cache, s);
-                    vfma(pb, a, pb, bb);
-                    vmul(pa, a, pa);
+                for (int ss = 0; ss < SR; ++ss) {
+                    const int s = P::REV ? (SR - 1 - ss) : ss;
+                    const int r = rg * SR + s;
+                    if (FULL || t0 + r < ka.T) {
+                        const char* rows[4];
+                        rows_at(r, rows);
+                        acc a[VEC], bb[VEC];
+                        step_coef<K, Tin, Te, SR>(rows, ka, a, bb, cache, s);
+                        vfma(pb, a, pb, bb);
+                        vmul(pa, a, pa);
+                    }
                 }
-            }
+            };
+            if (rg_full)
+                phase1(std::true_type{});
+            else
+                phase1(std::false_type{});
             // ---- warp: inclusive scan over row groups (shuffles) -----------
             acc ex_a[VEC], ex_b[VEC];  // first round's neighbour (RGW == 2: the exclusive prefix)
 #pragma unroll
@@ -329,18 +362,25 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
             char* const ob0 = ka.out[0].p + (orow0 * ka.out[0].rs + gc) * (int64_t)P::OES;
             char* const ob1 = ka.out[1].p + (orow0 * ka.out[1].rs + gc) * (int64_t)P::OES;
             const int64_t os0 = ka.out[0].rs * (int64_t)P::OES, os1 = ka.out[1].rs * (int64_t)P::OES;
+            auto phase3 = [&](auto full_tag) {
+                constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll
-            for (int ss = 0; ss < SR; ++ss) {
-                const int s = P::REV ? (SR - 1 - ss) : ss;
-                const int r = rg * SR + s;
-                const int64_t t = t0 + r;
-                if (t < ka.T) {
-                    const char* rows[4];
-                    rows_at(r, rows);
-                    step_apply<K, Tin, Te, SR>(rows, ka, b, t, gc, valid, e, cache, s, ob0 + s * os0,
-                                               ob1 + s * os1);
+                for (int ss = 0; ss < SR; ++ss) {
+                    const int s = P::REV ? (SR - 1 - ss) : ss;
+                    const int r = rg * SR + s;
+                    const int64_t t = t0 + r;
+                    if (FULL || t < ka.T) {
+                        const char* rows[4];
+                        rows_at(r, rows);
+                        step_apply<K, Tin, Te, SR>(rows, ka, b, t, gc, valid, e, cache, s, ob0 + s * os0,
+                                                   ob1 + s * os1);
+                    }
                 }
-            }
+            };
+            if (rg_full)
+                phase3(std::true_type{});
+            else
+                phase3(std::false_type{});
             }
             if (last_rg) sts_planar<acc, VEC, LPR>(carry + (cur ^ 1) * WS, cl, e);
             // stage `slot` consumed, next carry visible; the whole CTA stops if
@@ -350,10 +390,17 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
                 break;
             }
             if (j + nstage < prm.ntt) {
-                if (threadIdx.x == 0)
+                if (threadIdx.x == 0) {
+                    if (prm.prefetch > 0 && j + nstage + prm.prefetch < prm.ntt)
+                        strip_prefetch<Cfg>(prm, maps, b, strip, tile_t0(j + nstage + prm.prefetch));
                     strip_issue<Cfg>(prm, maps, smem + (size_t)slot * Cfg::stage_bytes(), &bars[slot],
                                      b, strip, tile_t0(j + nstage), policy);
+                }
                 ++issued;
+            }
+            if (++slot == nstage) {
+                slot = 0;
+                parity ^= 1u;
             }
         }
         if (aborted) break;
@@ -379,6 +426,17 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
         mbar_wait_bounded(&bars[u % nstage], (unsigned)((u / nstage) & 1), ka.status);
 }
 
+// Tuning overrides read once from the environment (0 = automatic):
+// ESA_STRIP_LPR (4/8/16/32 lanes per row), ESA_STRIP_STAGES (2..8) and
+// ESA_STRIP_PREFETCH (n: n-1 tiles of L2 prefetch ahead of the ring).
+inline int strip_env(const char* name) {
+    const char* v = getenv(name);
+    return v ? atoi(v) : 0;
+}
+
+// Tiles each CTA keeps in flight into L2 beyond its shared-memory ring.
+constexpr int kStripPrefetchTiles = 0;
+
 // Build a 3-D tensor map [nb][T][hd] (row stride rs elements) with box
 // [1][LT][WS] for dtype code `dtype`.
 bool encode_strip_map(CUtensorMap* map, int dtype, const void* base, int64_t nb, int64_t T,
@@ -394,6 +452,8 @@ int strip_launch_typed(const ScanCall& call, int nstage, int grid) {
     prm.nitems = call.a.nb * prm.spr;
     prm.ntt = (call.a.T + Cfg::LT - 1) / Cfg::LT;
     prm.nstage = nstage;
+    static const int env_pf = strip_env("ESA_STRIP_PREFETCH");
+    prm.prefetch = env_pf > 0 ? env_pf - 1 : kStripPrefetchTiles;
     CUtensorMap maps[4];
     memset(maps, 0, sizeof(maps));
     const int dts[4] = {
@@ -446,12 +506,6 @@ int strip_occupancy(int dev, int nstage) {
     return per_sm;
 }
 
-// Tuning overrides read once from the environment (0 = automatic):
-// ESA_STRIP_LPR (4/8/16/32 lanes per row) and ESA_STRIP_STAGES (2..8).
-inline int strip_env(const char* name) {
-    const char* v = getenv(name);
-    return v ? atoi(v) : 0;
-}
 
 // Picks the strip width (LPR) and pipeline depth for the call, or declines
 // (*taken = false) when the strips cannot fill the GPU (then the caller uses
