@@ -1,12 +1,12 @@
-"""Parity of the chained-piece strip scan (few channels, long time axis).
+"""Parity of the scan on few-channel, long-time-axis problems.
 
-With few channels per batch row the strip scan cuts every strip's time axis
-into pieces that run on different CTAs: an aggregate pass, a decoupled
-look-back over the earlier pieces and an output pass from the exact incoming
-state.  These shapes (2 to 8 strips, thousands of steps) always take that
-path.  Same bar as the other scan tests: relative Frobenius error against the
-fp64 oracle on the same rounded inputs -- 1e-5 fp32, 2e-3 fp16/bf16, 1e-12
-fp64.
+With few channels per batch row the strips cannot fill the GPU, so the time
+axis is split across CTAs (the time-parallel look-back scan: per-tile
+aggregates, a decoupled look-back over earlier tiles, outputs from the exact
+incoming state).  These shapes (2 to 8 strips' worth of channels, thousands of
+steps) exercise that split in every kind, with initial and final states.
+Same bar as the other scan tests: relative Frobenius error against the fp64
+oracle on the same rounded inputs -- 1e-5 fp32, 2e-3 fp16/bf16, 1e-12 fp64.
 """
 import numpy as np
 import pytest
