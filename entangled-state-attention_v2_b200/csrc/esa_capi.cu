@@ -80,9 +80,11 @@ ESA_EXPORT int esa_scan_fwd_host(const void* A, const void* B, void* E, int64_t 
 }
 
 ESA_EXPORT int esa_scan_summary(const void* A, const void* B, int64_t nb, int64_t T, int64_t hd,
-                                int dtype, const void* e0, void* e_last, void* prod, void* stream) {
+                                int dtype, const void* e0, void* e_last, void* prod, void* workspace,
+                                size_t workspace_bytes, void* stream) {
     clear_error();
-    return scan_summary(A, B, nb, T, hd, dtype, e0, e_last, prod, static_cast<cudaStream_t>(stream));
+    return scan_summary(A, B, nb, T, hd, dtype, e0, e_last, prod, workspace, workspace_bytes,
+                        static_cast<cudaStream_t>(stream));
 }
 
 ESA_EXPORT int esa_scan_rev(const void* A, const void* E, const void* dE, void* dA, void* dB, int64_t nb,

@@ -53,7 +53,8 @@ struct KArgs {
     int64_t nb, T, hd;
     const void* e0;    // acc [nb*hd] or null
     void* e_last;      // fwd: E_{T-1}; rev: gradient w.r.t. e0 (acc [nb*hd]) or null
-    void* prod_out;    // FwdSummary: product of A over [0, T) (acc [nb*hd])
+    void* prod_out;    // summary passes: product of the step coefficients (acc [rows*hd])
+    const void* cin;   // split passes: incoming state per (row, piece) (acc [nb*npiece*hd]) or null
     double gmin, span; // gate_min and gate_max - gate_min
     int round_ab;
     unsigned* status;  // device status word
@@ -69,6 +70,10 @@ struct ScanCall {
     size_t ws_bytes;
     cudaStream_t stream;
     bool bulk_ok;  // every row 16-byte aligned (TMA-stageable)
+    // time split: each batch row cut into npiece pieces of plen steps (a
+    // multiple of 64), processed as independent rows of the strip scan
+    int64_t npiece = 1, plen = 0;
+    bool summ = false;  // summary pass: end state and coefficient product, no outputs
 };
 
 // Channel-strip scan (no inter-CTA waits).  Sets *taken = false when the
@@ -95,7 +100,7 @@ int gated_scan_bwd(const void* g, const void* v, int64_t rrs, int raw_dtype, con
                    int compass, const void* e0, void* de0, void* ws, size_t ws_bytes,
                    cudaStream_t s);
 int scan_summary(const void* A, const void* B, int64_t nb, int64_t T, int64_t hd, int dtype,
-                 const void* e0, void* e_last, void* prod, cudaStream_t s);
+                 const void* e0, void* e_last, void* prod, void* ws, size_t ws_bytes, cudaStream_t s);
 size_t scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int compass);
 size_t scan_host_staging_bytes(int64_t nb, int64_t T, int64_t hd, int es, int compass);
 int scan_fwd_host(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd, int dtype,

@@ -4,8 +4,13 @@
 // Path choice for every scan kind:
 //   1. strip scan (esa_strip.cuh) when every row is 16-byte aligned and there
 //      are enough channels to fill the GPU with channel strips;
-//   2. otherwise the time-parallel lookback scan (esa_scan_lookback.cu);
-//   3. rows that are not 16-byte aligned (odd channel counts, offset views):
+//   2. few channels and a long time axis: the split scan -- every batch row
+//      cut into time pieces that the strip scan treats as rows: a summary
+//      pass (each piece's end state from zero and its coefficient product),
+//      a composition of the pieces' incoming states in time order (one
+//      thread per channel), and the output pass from those exact states;
+//   3. otherwise the time-parallel lookback scan (esa_scan_lookback.cu);
+//   4. rows that are not 16-byte aligned (odd channel counts, offset views):
 //      one thread per channel, sequential over time.
 #include <cudaTypedefs.h>
 
@@ -21,8 +26,10 @@ int strip_rev_plain(const ScanCall& c, bool* taken);
 int strip_fwd_gated(const ScanCall& c, bool* taken);
 int strip_rev_gated(const ScanCall& c, bool* taken);
 int strip_fwd_summary(const ScanCall& c, bool* taken);
+int strip_summary_launch(const ScanCall& c, bool* taken);
 
 int strip_scan_launch(const ScanCall& c, bool* taken) {
+    if (c.summ) return strip_summary_launch(c, taken);
     switch (c.kind) {
         case Kind::FwdPlain: return strip_fwd_plain(c, taken);
         case Kind::RevPlain: return strip_rev_plain(c, taken);
@@ -215,6 +222,8 @@ int check_dims(int64_t nb, int64_t T, int64_t hd, int compass) {
     return ESA_OK;
 }
 
+int run_split(ScanCall& c, bool* done);
+
 int run(ScanCall& c) {
     if (c.a.nb == 0 || c.a.T == 0 || c.a.hd == 0) return ESA_OK;
     int dev = 0;
@@ -222,6 +231,9 @@ int run(ScanCall& c) {
     c.a.status = status_ptr(dev);
     if (c.a.status == nullptr) return set_error(ESA_ERR_CUDA, "cannot resolve the device status word");
     if (!c.bulk_ok) return sequential_scan_launch(c);
+    bool done = false;
+    if (int rc = run_split(c, &done)) return rc;
+    if (done) return ESA_OK;
     bool taken = false;
     const int rc = strip_scan_launch(c, &taken);
     if (rc != ESA_OK || taken) return rc;
@@ -230,10 +242,159 @@ int run(ScanCall& c) {
     return lookback_scan_launch(c);
 }
 
+// ---- split scan -------------------------------------------------------------
+
+struct SplitPlan {
+    int64_t npiece = 1, plen = 0;
+};
+
+// Pieces per batch row for an [nb, T, hd] problem whose widest element has
+// `wide_es` bytes: split when 128-channel-wide strips (16 lanes) number fewer
+// than one per SM of a B200 and the time axis is long (>= 8192 steps; shorter
+// problems do better on the look-back scan, measured).  Aim at about 2400
+// strip-pieces (eight waves of 2 CTAs on 148 SMs, so the last wave's
+// imbalance is small) with pieces of at least 1024 steps, a multiple of 64
+// steps (every strip tile length divides 64).
+SplitPlan split_plan(int64_t nb, int64_t T, int64_t hd, int wide_es) {
+    SplitPlan p;
+    if (wide_es <= 0 || T < 8192) return p;
+    const int64_t ws16 = 16 * (16 / wide_es);
+    const int64_t strips16 = nb * ((hd + ws16 - 1) / ws16);
+    if (strips16 <= 0 || strips16 >= 148) return p;
+    int64_t n = (2400 + strips16 - 1) / strips16;
+    // within 1/8 of that, the piece count whose strip-pieces fill whole waves
+    // of 296 (2 CTAs on 148 SMs) best
+    {
+        int64_t best_n = n;
+        double best_fill = 0.0;
+        for (int64_t m = n - n / 8; m <= n + n / 8; ++m) {
+            if (m < 2) continue;
+            const int64_t items = strips16 * m;
+            const double fill = (double)items / (double)(((items + 295) / 296) * 296);
+            if (fill > best_fill + 1e-9) {
+                best_fill = fill;
+                best_n = m;
+            }
+        }
+        n = best_n;
+    }
+    if (n > T / 1024) n = T / 1024;
+    if (n < 2) return p;
+    const int64_t plen = ((T + n - 1) / n + 63) / 64 * 64;
+    p.npiece = (T + plen - 1) / plen;
+    p.plen = plen;
+    if (p.npiece < 2) p.npiece = 1;
+    return p;
+}
+
+size_t split_plane_bytes(int64_t nb, const SplitPlan& p, int64_t hd, size_t acc_size) {
+    return ((size_t)(nb * p.npiece * hd) * acc_size + 255) / 256 * 256;
+}
+
+// Incoming state of every (batch row, piece) from the pieces' summaries, in
+// time order (reverse kinds: descending), one thread per channel; the state
+// after the last piece goes to e_last, the product over all pieces to
+// prod_total (either may be null).
+template <typename acc>
+__global__ void compose_pieces_kernel(const acc* __restrict__ prod, const acc* __restrict__ endst,
+                                      const acc* __restrict__ e0, acc* __restrict__ cin,
+                                      acc* __restrict__ e_last, acc* __restrict__ prod_total,
+                                      int64_t nb, int64_t npiece, int64_t hd, int rev) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= nb * hd) return;
+    const int64_t b = idx / hd, ch = idx - b * hd;
+    acc st = (e0 != nullptr && !rev) ? e0[idx] : acc(0);
+    acc pr = acc(1);
+    for (int64_t q = 0; q < npiece; ++q) {
+        const int64_t p = rev ? npiece - 1 - q : q;
+        const int64_t o = (b * npiece + p) * hd + ch;
+        cin[o] = st;
+        const acc a = prod[o];
+        st = a * st + endst[o];
+        pr = pr * a;
+    }
+    if (e_last != nullptr) e_last[idx] = st;
+    if (prod_total != nullptr) prod_total[idx] = pr;
+}
+
+int wide_size(const ScanCall& c) {
+    const int a = dtype_size(c.tin), b = dtype_size(c.te);
+    return a > b ? a : b;
+}
+
+// The split scan for few-channel, long problems; *done = false (nothing
+// launched) when the problem is not split or the workspace is too small.
+int run_split(ScanCall& c, bool* done) {
+    *done = false;
+    const int wes = wide_size(c);
+    const SplitPlan sp = split_plan(c.a.nb, c.a.T, c.a.hd, wes);
+    if (sp.npiece < 2) return ESA_OK;
+    const size_t acc_size = wes == 8 ? 8 : 4;
+    const size_t plane = split_plane_bytes(c.a.nb, sp, c.a.hd, acc_size);
+    if (c.ws == nullptr || c.ws_bytes < 3 * plane || (reinterpret_cast<uintptr_t>(c.ws) & 255u)) return ESA_OK;
+    char* ws = static_cast<char*>(c.ws);
+    void* prod = ws;
+    void* endst = ws + plane;
+    void* cin = ws + 2 * plane;
+    const bool rev = c.kind == Kind::RevPlain || c.kind == Kind::RevGated;
+
+    // pass 1: summaries of every piece from a zero state
+    ScanCall c1 = c;
+    c1.npiece = sp.npiece;
+    c1.plen = sp.plen;
+    c1.summ = true;
+    c1.a.e0 = nullptr;
+    c1.a.cin = nullptr;
+    c1.a.e_last = endst;
+    c1.a.prod_out = prod;
+    c1.ws = nullptr;
+    c1.ws_bytes = 0;
+    bool taken = false;
+    if (int rc = strip_scan_launch(c1, &taken)) return rc;
+    if (!taken) return ESA_OK;
+    // pass 2: incoming states in time order
+    const int64_t n = c.a.nb * c.a.hd;
+    const int threads = 256;
+    const unsigned blocks = (unsigned)((n + threads - 1) / threads);
+    const bool summary = c.kind == Kind::FwdSummary;
+    if (acc_size == 8) {
+        compose_pieces_kernel<double><<<blocks, threads, 0, c.stream>>>(
+            static_cast<const double*>(prod), static_cast<const double*>(endst),
+            static_cast<const double*>(rev ? nullptr : c.a.e0), static_cast<double*>(cin),
+            static_cast<double*>(c.a.e_last), static_cast<double*>(summary ? c.a.prod_out : nullptr),
+            c.a.nb, sp.npiece, c.a.hd, rev ? 1 : 0);
+    } else {
+        compose_pieces_kernel<float><<<blocks, threads, 0, c.stream>>>(
+            static_cast<const float*>(prod), static_cast<const float*>(endst),
+            static_cast<const float*>(rev ? nullptr : c.a.e0), static_cast<float*>(cin),
+            static_cast<float*>(c.a.e_last), static_cast<float*>(summary ? c.a.prod_out : nullptr),
+            c.a.nb, sp.npiece, c.a.hd, rev ? 1 : 0);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("piece composition: ") + cudaGetErrorString(e));
+    *done = true;
+    if (summary) return ESA_OK;
+    // pass 3: outputs from each piece's exact incoming state
+    ScanCall c3 = c;
+    c3.npiece = sp.npiece;
+    c3.plen = sp.plen;
+    c3.a.cin = cin;
+    c3.a.e_last = nullptr;
+    c3.ws = nullptr;
+    c3.ws_bytes = 0;
+    taken = false;
+    if (int rc = strip_scan_launch(c3, &taken)) return rc;
+    if (!taken) return set_error(ESA_ERR_CUDA, "split scan: output pass not launched");
+    return ESA_OK;
+}
+
 }  // namespace
 
 size_t scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int compass) {
-    return lookback_workspace_bytes(nb, T, hd, wide_es, compass);
+    const size_t lb = lookback_workspace_bytes(nb, T, hd, wide_es, compass);
+    const SplitPlan sp = split_plan(nb, T, hd, wide_es);
+    const size_t split = sp.npiece > 1 ? 3 * split_plane_bytes(nb, sp, hd, wide_es == 8 ? 8 : 4) : 0;
+    return lb > split ? lb : split;
 }
 
 int scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd, int dtype,
@@ -262,7 +423,7 @@ int scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64
 }
 
 int scan_summary(const void* A, const void* B, int64_t nb, int64_t T, int64_t hd, int dtype,
-                 const void* e0, void* e_last, void* prod, cudaStream_t s) {
+                 const void* e0, void* e_last, void* prod, void* ws, size_t ws_bytes, cudaStream_t s) {
     if (int rc = check_dims(nb, T, hd, 16)) return rc;
     const int es = dtype_size(dtype);
     if (es == 0) return set_error(ESA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code " + std::to_string(dtype));
@@ -280,6 +441,8 @@ int scan_summary(const void* A, const void* B, int64_t nb, int64_t T, int64_t hd
     c.a.e_last = e_last;
     c.a.prod_out = prod;
     c.compass = 16;
+    c.ws = ws;
+    c.ws_bytes = ws_bytes;
     c.stream = s;
     c.bulk_ok = rows_aligned(A, hd, hd, es) && rows_aligned(B, hd, hd, es);
     return run(c);

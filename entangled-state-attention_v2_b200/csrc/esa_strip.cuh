@@ -43,11 +43,11 @@ namespace esa {
 
 struct StripParams {
     KArgs a;
-    int64_t spr;     // strips per batch row = ceil(hd / WS)
-    int64_t nitems;  // nb * spr
-    int64_t ntt;     // tiles along T = ceil(T / LT)
+    int64_t spr;     // strips per (batch row, piece) = ceil(hd / WS)
+    int64_t nitems;  // nb * npiece * spr
+    int64_t npiece;  // time pieces per batch row (1: the whole axis)
+    int64_t plen;    // steps per piece (a multiple of LT; >= T when npiece == 1)
     int nstage;
-    int prefetch;    // tiles prefetched into L2 ahead of the shared-memory ring
 };
 
 template <Kind K, typename Tin, typename Te, int LPR_, int SR_>
@@ -84,22 +84,6 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
         ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;"
         :: "r"(d), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(b), "l"(policy)
         : "memory");
-}
-
-// L2 prefetch of one tile (no shared memory, no completion): raises the
-// bytes in flight from DRAM beyond what the shared-memory ring holds.
-__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, int y, int z) {
-    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];"
-                 :: "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z) : "memory");
-}
-
-template <class Cfg>
-__device__ __forceinline__ void strip_prefetch(const StripParams& prm, const CUtensorMap* const (&maps)[4],
-                                               int64_t b, int64_t strip, int64_t t0) {
-    using P = typename Cfg::P;
-#pragma unroll
-    for (int a = 0; a < P::NIN; ++a)
-        tma_prefetch_3d(maps[a], (int)(strip * Cfg::WS), (int)(t0 + P::shift(a)), (int)b);
 }
 
 template <class Cfg>
@@ -140,7 +124,7 @@ __device__ __forceinline__ void sts_planar(A* row, int cl, const A (&in)[N]) {
     }
 }
 
-template <Kind K, typename Tin, typename Te, int LPR, int SR>
+template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM_>
 __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams prm,
                                                          const __grid_constant__ CUtensorMap m0,
                                                          const __grid_constant__ CUtensorMap m1,
@@ -155,6 +139,9 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
     constexpr int RGW = Cfg::RGW;
     constexpr int LT = Cfg::LT;
     constexpr unsigned FULL = 0xffffffffu;
+    // summary pass: no per-step outputs; the end state of each (row, piece)
+    // from its incoming state and the product of its step coefficients
+    constexpr bool SUMM = SUMM_ || K == Kind::FwdSummary;
     const KArgs& ka = prm.a;
     const int nstage = prm.nstage;
 
@@ -192,41 +179,70 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
     int slot = 0;         // ring stage of the next tile to consume (= used % nstage)
     unsigned parity = 0;  // its mbarrier phase parity (= (used / nstage) & 1)
     bool aborted = false;
+    // tiles of the current item already issued by the previous item's tail
+    // (the ring runs on into the next item of this CTA without draining)
+    int pre = 0;
+    // geometry of an item: (batch row, piece) row, strip, piece start, tiles
+    struct ItemGeom {
+        int64_t row, strip, b, pbeg, pend, ntt;
+    };
+    auto geom = [&](int64_t it) {
+        ItemGeom g;
+        g.row = it / prm.spr;
+        g.strip = it - g.row * prm.spr;
+        g.b = g.row / prm.npiece;
+        g.pbeg = (g.row - g.b * prm.npiece) * prm.plen;
+        g.pend = g.pbeg + prm.plen < ka.T ? g.pbeg + prm.plen : ka.T;
+        g.ntt = (g.pend - g.pbeg + LT - 1) / LT;
+        return g;
+    };
+    auto geom_t0 = [&](const ItemGeom& g, int64_t j) -> int64_t {
+        return g.pbeg + (P::REV ? (g.ntt - 1 - j) : j) * (int64_t)LT;
+    };
     for (int64_t item = blockIdx.x; item < prm.nitems && !aborted; item += gridDim.x) {
-        const int64_t b = item / prm.spr;
-        const int64_t strip = item - b * prm.spr;
+        const ItemGeom ig = geom(item);
+        const int64_t row = ig.row;  // (batch row, piece)
+        const int64_t strip = ig.strip;
+        const int64_t b = ig.b;
+        const int64_t pend = ig.pend;
+        const int64_t ntt = ig.ntt;  // tiles of the piece
         const int64_t gc = strip * WS + c;  // first global channel of this thread
         const bool valid = gc < ka.hd;
-        auto tile_t0 = [&](int64_t j) -> int64_t {
-            return (P::REV ? (prm.ntt - 1 - j) : j) * (int64_t)LT;
-        };
+        auto tile_t0 = [&](int64_t j) -> int64_t { return geom_t0(ig, j); };
+        // the next item of this CTA, whose first tiles this item's tail issues
+        const int64_t next = item + gridDim.x;
+        const bool has_next = next < prm.nitems && ntt >= nstage;
+        const ItemGeom ng = geom(has_next ? next : item);
+        const int next_pre = has_next ? (int)(ng.ntt < nstage ? ng.ntt : nstage) : 0;
         acc prod_run[VEC];  // FwdSummary: product of A so far (last row group's lanes)
 #pragma unroll
         for (int i = 0; i < VEC; ++i) prod_run[i] = acc(1);
-        // initial carry: e0 (forward) or zero (reverse: nothing after T)
+        // initial carry: the piece's incoming state (split passes), else e0
+        // (forward) or zero (reverse: nothing after T)
         if (rgl == 0 && warp == 0) {
             acc x[VEC];
+            const acc* src = ka.cin != nullptr ? static_cast<const acc*>(ka.cin) + row * ka.hd + gc
+                             : (!P::REV && ka.e0 != nullptr) ? static_cast<const acc*>(ka.e0) + b * ka.hd + gc
+                                                             : nullptr;
 #pragma unroll
-            for (int i = 0; i < VEC; ++i)
-                x[i] = (!P::REV && ka.e0 != nullptr && valid) ? static_cast<const acc*>(ka.e0)[b * ka.hd + gc + i]
-                                                              : acc(0);
+            for (int i = 0; i < VEC; ++i) x[i] = (src != nullptr && valid) ? src[i] : acc(0);
             sts_planar<acc, VEC, LPR>(carry, cl, x);  // slot 0
         }
         // prologue: fill the ring
-        const int npro = (int)(prm.ntt < nstage ? prm.ntt : nstage);
+        const int npro = (int)(ntt < nstage ? ntt : nstage);
         if (threadIdx.x == 0) {
-            for (int s = npro; s < npro + prm.prefetch && s < prm.ntt; ++s)
-                strip_prefetch<Cfg>(prm, maps, b, strip, tile_t0(s));
-            for (int s = 0, sl = slot; s < npro; ++s) {
+            int sl = slot + pre;
+            if (sl >= nstage) sl -= nstage;
+            for (int s = pre; s < npro; ++s) {
                 strip_issue<Cfg>(prm, maps, smem + (size_t)sl * Cfg::stage_bytes(), &bars[sl], b,
                                  strip, tile_t0(s), policy);
                 if (++sl == nstage) sl = 0;
             }
         }
-        issued += npro;
+        issued += npro > pre ? npro - pre : 0;
         __syncthreads();
 
-        for (int64_t j = 0; j < prm.ntt; ++j, ++used) {
+        for (int64_t j = 0; j < ntt; ++j, ++used) {
             const int cur = (int)(j & 1);
             const int64_t t0 = tile_t0(j);
             const bool ok = mbar_wait_bounded(&bars[slot], parity, ka.status);
@@ -248,14 +264,14 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
             }
             // every step of this row group inside [0, T) (all but the last tile):
             // the step loops run without per-step bounds checks
-            const bool rg_full = t0 + (rg + 1) * SR <= ka.T;
+            const bool rg_full = t0 + (rg + 1) * SR <= pend;
             auto phase1 = [&](auto full_tag) {
                 constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll
                 for (int ss = 0; ss < SR; ++ss) {
                     const int s = P::REV ? (SR - 1 - ss) : ss;
                     const int r = rg * SR + s;
-                    if (FULL || t0 + r < ka.T) {
+                    if (FULL || t0 + r < pend) {
                         const char* rows[4];
                         rows_at(r, rows);
                         acc a[VEC], bb[VEC];
@@ -346,7 +362,7 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
             acc e[VEC];
             lds_planar<acc, VEC, LPR>(carry + cur * WS, cl, e);
             vfma(e, ea, e, eb);  // through the warps before this one
-            if constexpr (K == Kind::FwdSummary) {
+            if constexpr (SUMM) {
                 // no per-step outputs: the last row group's warp-inclusive pair
                 // carries the state to the tile end; the product of A follows
                 if (last_rg) {
@@ -369,7 +385,7 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
                     const int s = P::REV ? (SR - 1 - ss) : ss;
                     const int r = rg * SR + s;
                     const int64_t t = t0 + r;
-                    if (FULL || t < ka.T) {
+                    if (FULL || t < pend) {
                         const char* rows[4];
                         rows_at(r, rows);
                         step_apply<K, Tin, Te, SR>(rows, ka, b, t, gc, valid, e, cache, s, ob0 + s * os0,
@@ -389,13 +405,16 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
                 aborted = true;
                 break;
             }
-            if (j + nstage < prm.ntt) {
-                if (threadIdx.x == 0) {
-                    if (prm.prefetch > 0 && j + nstage + prm.prefetch < prm.ntt)
-                        strip_prefetch<Cfg>(prm, maps, b, strip, tile_t0(j + nstage + prm.prefetch));
+            if (j + nstage < ntt) {
+                if (threadIdx.x == 0)
                     strip_issue<Cfg>(prm, maps, smem + (size_t)slot * Cfg::stage_bytes(), &bars[slot],
                                      b, strip, tile_t0(j + nstage), policy);
-                }
+                ++issued;
+            } else if (j + nstage - ntt < next_pre) {
+                // the freed stage takes the next item's tile j + nstage - ntt
+                if (threadIdx.x == 0)
+                    strip_issue<Cfg>(prm, maps, smem + (size_t)slot * Cfg::stage_bytes(), &bars[slot],
+                                     ng.b, ng.strip, geom_t0(ng, j + nstage - ntt), policy);
                 ++issued;
             }
             if (++slot == nstage) {
@@ -404,20 +423,21 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
             }
         }
         if (aborted) break;
-        if constexpr (K == Kind::FwdSummary) {
+        if constexpr (SUMM) {
             if (last_rg && valid) {
 #pragma unroll
-                for (int i = 0; i < VEC; ++i) static_cast<acc*>(ka.prod_out)[b * ka.hd + gc + i] = prod_run[i];
+                for (int i = 0; i < VEC; ++i) static_cast<acc*>(ka.prod_out)[row * ka.hd + gc + i] = prod_run[i];
             }
         }
         // final state: E_{T-1} (forward) or the gradient w.r.t. e0 (reverse)
         if (ka.e_last != nullptr && rgl == 0 && warp == 0 && valid) {
-            const int fin = (int)(prm.ntt & 1);
+            const int fin = (int)(ntt & 1);
             acc x[VEC];
             lds_planar<acc, VEC, LPR>(carry + fin * WS, cl, x);
 #pragma unroll
-            for (int i = 0; i < VEC; ++i) static_cast<acc*>(ka.e_last)[b * ka.hd + gc + i] = x[i];
+            for (int i = 0; i < VEC; ++i) static_cast<acc*>(ka.e_last)[row * ka.hd + gc + i] = x[i];
         }
+        pre = next_pre;
         __syncthreads();
     }
     // after a failed wait, give every copy still in flight one more bounded
@@ -427,33 +447,29 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
 }
 
 // Tuning overrides read once from the environment (0 = automatic):
-// ESA_STRIP_LPR (4/8/16/32 lanes per row), ESA_STRIP_STAGES (2..8) and
-// ESA_STRIP_PREFETCH (n: n-1 tiles of L2 prefetch ahead of the ring).
+// ESA_STRIP_LPR (4/8/16/32 lanes per row) and ESA_STRIP_STAGES (2..8).
 inline int strip_env(const char* name) {
     const char* v = getenv(name);
     return v ? atoi(v) : 0;
 }
-
-// Tiles each CTA keeps in flight into L2 beyond its shared-memory ring.
-constexpr int kStripPrefetchTiles = 0;
 
 // Build a 3-D tensor map [nb][T][hd] (row stride rs elements) with box
 // [1][LT][WS] for dtype code `dtype`.
 bool encode_strip_map(CUtensorMap* map, int dtype, const void* base, int64_t nb, int64_t T,
                       int64_t hd, int64_t rs, int ws, int lt, std::string* err);
 
-template <Kind K, typename Tin, typename Te, int LPR, int SR>
+template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM>
 int strip_launch_typed(const ScanCall& call, int nstage, int grid) {
     using Cfg = StripCfg<K, Tin, Te, LPR, SR>;
     using P = typename Cfg::P;
     StripParams prm{};
     prm.a = call.a;
     prm.spr = (call.a.hd + Cfg::WS - 1) / Cfg::WS;
-    prm.nitems = call.a.nb * prm.spr;
-    prm.ntt = (call.a.T + Cfg::LT - 1) / Cfg::LT;
+    prm.npiece = call.npiece > 1 ? call.npiece : 1;
+    prm.plen = prm.npiece > 1 ? call.plen : ((call.a.T + Cfg::LT - 1) / Cfg::LT) * Cfg::LT;
+    if (prm.plen % Cfg::LT != 0) return set_error(ESA_ERR_INVALID_ARGUMENT, "piece length not a multiple of the tile");
+    prm.nitems = call.a.nb * prm.npiece * prm.spr;
     prm.nstage = nstage;
-    static const int env_pf = strip_env("ESA_STRIP_PREFETCH");
-    prm.prefetch = env_pf > 0 ? env_pf - 1 : kStripPrefetchTiles;
     CUtensorMap maps[4];
     memset(maps, 0, sizeof(maps));
     const int dts[4] = {
@@ -470,11 +486,11 @@ int strip_launch_typed(const ScanCall& call, int nstage, int grid) {
             return set_error(ESA_ERR_CUDA, "tensor map: " + err);
     }
     const size_t smem = Cfg::smem_bytes(nstage);
-    cudaError_t e = cudaFuncSetAttribute(strip_scan_kernel<K, Tin, Te, LPR, SR>,
+    cudaError_t e = cudaFuncSetAttribute(strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("strip smem attribute: ") + cudaGetErrorString(e));
     if (grid > prm.nitems) grid = (int)prm.nitems;
-    strip_scan_kernel<K, Tin, Te, LPR, SR><<<grid, Cfg::NT, smem, call.stream>>>(prm, maps[0], maps[1],
+    strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM><<<grid, Cfg::NT, smem, call.stream>>>(prm, maps[0], maps[1],
                                                                                   maps[2], maps[3]);
     e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("strip scan launch: ") + cudaGetErrorString(e));
@@ -483,7 +499,7 @@ int strip_launch_typed(const ScanCall& call, int nstage, int grid) {
 
 // Occupancy (CTAs per SM) of a strip configuration with `nstage` stages
 // (cached per device and stage count; 0 if it cannot be resident).
-template <Kind K, typename Tin, typename Te, int LPR, int SR>
+template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM>
 int strip_occupancy(int dev, int nstage) {
     using Cfg = StripCfg<K, Tin, Te, LPR, SR>;
     static int cache[16][9];  // [device][nstage]: 0 unknown, -1 none, else occupancy
@@ -493,9 +509,9 @@ int strip_occupancy(int dev, int nstage) {
     const size_t smem = Cfg::smem_bytes(nstage);
     int per_sm = 0;
     if (smem <= 232448 &&
-        cudaFuncSetAttribute(strip_scan_kernel<K, Tin, Te, LPR, SR>,
+        cudaFuncSetAttribute(strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, strip_scan_kernel<K, Tin, Te, LPR, SR>,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM>,
                                                       Cfg::NT, smem) == cudaSuccess &&
         per_sm > 0) {
         slot = per_sm;
@@ -509,19 +525,19 @@ int strip_occupancy(int dev, int nstage) {
 
 // Picks the strip width (LPR) and pipeline depth for the call, or declines
 // (*taken = false) when the strips cannot fill the GPU (then the caller uses
-// the time-parallel lookback scan).  Among configurations that keep every
-// strip resident in one wave (no tail wave), prefer
-//   1. at least two CTAs per SM (a lone 8-warp CTA cannot hide the per-tile
-//      barriers and shared-memory round trips);
-//   2. wider strips (longer DRAM rows, fewer CTAs);
-//   3. the most stages that fit (measured: 2 to 6 stages perform alike).
-template <Kind K, typename Tin, typename Te, int SR4, int SR8, int SR16, int SR32>
+// the time-parallel lookback scan).  Each width is scored by load balance
+// (strips over SMs in one wave, or waves over the resident CTAs) x 0.6 when
+// SMs would hold a single CTA x a short-row penalty (0.97 for 128-byte rows,
+// 0.9 for 64-byte rows); ties go to the wider strip.  Stages: the most that
+// keep two CTAs per SM (measured: 2 to 6 stages perform alike).
+template <Kind K, typename Tin, typename Te, int SR4, int SR8, int SR16, int SR32, bool SUMM = false>
 int strip_launch_kind(const ScanCall& call, bool* taken) {
     *taken = false;
     int dev = 0;
     cudaGetDevice(&dev);
     const int sms = device_sm_count(dev);
-    const int64_t T = call.a.T, nb = call.a.nb, hd = call.a.hd;
+    // rows of the strip scan: batch rows x time pieces
+    const int64_t T = call.a.T, nb = call.a.nb * (call.npiece > 1 ? call.npiece : 1), hd = call.a.hd;
     using P = Policy<K, Tin, Te>;
     if (T < 16) return ESA_OK;
     static const int force_lpr = strip_env("ESA_STRIP_LPR");
@@ -529,45 +545,52 @@ int strip_launch_kind(const ScanCall& call, bool* taken) {
     auto strips = [&](int lpr) { return nb * ((hd + lpr * P::VEC - 1) / (lpr * P::VEC)); };
     auto occ = [&](int lpr, int ns) -> int {
         switch (lpr) {
-            case 32: return strip_occupancy<K, Tin, Te, 32, SR32>(dev, ns);
-            case 16: return strip_occupancy<K, Tin, Te, 16, SR16>(dev, ns);
-            case 8: return strip_occupancy<K, Tin, Te, 8, SR8>(dev, ns);
-            default: return strip_occupancy<K, Tin, Te, 4, SR4>(dev, ns);
+            case 32: return strip_occupancy<K, Tin, Te, 32, SR32, SUMM>(dev, ns);
+            case 16: return strip_occupancy<K, Tin, Te, 16, SR16, SUMM>(dev, ns);
+            case 8: return strip_occupancy<K, Tin, Te, 8, SR8, SUMM>(dev, ns);
+            default: return strip_occupancy<K, Tin, Te, 4, SR4, SUMM>(dev, ns);
         }
     };
     int pick_lpr = 0, pick_ns = 0, pick_occ = 0;
-    int64_t best = -1;
+    double best = 0.0;
     for (int lpr : {32, 16, 8, 4}) {
         if (force_lpr && lpr != force_lpr) continue;
         const int64_t n = strips(lpr);
         if (n < (sms * 3) / 4) continue;  // too few strips to fill the GPU
-        const int64_t per_sm = (n + sms - 1) / sms;
-        for (int ns = 6; ns >= 2; --ns) {
-            if (force_ns && ns != force_ns) continue;
-            const int o = occ(lpr, ns);
-            if (o <= 0 || o < per_sm) continue;
-            // score: two or more CTAs per SM, then width
-            const int64_t score = (per_sm >= 2 ? 100 : 0) + lpr;
-            if (score > best) {
-                best = score;
-                pick_lpr = lpr;
-                pick_ns = ns;
-                pick_occ = o;
+        // the most stages that keep two CTAs per SM (else the best occupancy)
+        int ns = 0, o = 0;
+        for (int s = 6; s >= 2; --s) {
+            if (force_ns && s != force_ns) continue;
+            const int os = occ(lpr, s);
+            if (os > o) {
+                o = os;
+                ns = s;
             }
-            break;  // the most stages that fit is the best for this width
+            if (o >= 2) break;
         }
-    }
-    if (pick_lpr == 0) {
-        // more strips than can be resident at once: 2 stages, persistent CTAs
-        for (int lpr : {8, 16, 32, 4}) {
-            if (force_lpr && lpr != force_lpr) continue;
-            const int o = occ(lpr, 2);
-            if (strips(lpr) >= (sms * 3) / 4 && o > 0) {
-                pick_lpr = lpr;
-                pick_ns = 2;
-                pick_occ = o;
-                break;
-            }
+        if (o <= 0) continue;
+        const int64_t slots = (int64_t)o * sms;
+        // load balance: one wave spread over the SMs, or waves over the slots
+        double balance;
+        int64_t per_sm;
+        if (n <= slots) {
+            per_sm = (n + sms - 1) / sms;
+            balance = (double)n / (double)(per_sm * sms);
+        } else {
+            per_sm = o;
+            const int64_t waves = (n + slots - 1) / slots;
+            balance = (double)n / (double)(waves * slots);
+        }
+        // a lone 8-warp CTA per SM cannot hide the per-tile barriers and
+        // shared-memory round trips; 64-byte rows make short DRAM bursts
+        const double conc = per_sm >= 2 ? 1.0 : 0.6;
+        const double width = lpr >= 16 ? 1.0 : (lpr == 8 ? 0.97 : 0.9);
+        const double score = balance * conc * width;
+        if (score > best + 1e-9) {
+            best = score;
+            pick_lpr = lpr;
+            pick_ns = ns;
+            pick_occ = o;
         }
     }
     if (pick_lpr == 0) return ESA_OK;  // too few channels for strips: not taken
@@ -576,10 +599,10 @@ int strip_launch_kind(const ScanCall& call, bool* taken) {
     const int64_t cap = (int64_t)pick_occ * sms;
     const int grid = (int)(n < cap ? n : cap);
     switch (pick_lpr) {
-        case 32: return strip_launch_typed<K, Tin, Te, 32, SR32>(call, pick_ns, grid);
-        case 16: return strip_launch_typed<K, Tin, Te, 16, SR16>(call, pick_ns, grid);
-        case 8: return strip_launch_typed<K, Tin, Te, 8, SR8>(call, pick_ns, grid);
-        default: return strip_launch_typed<K, Tin, Te, 4, SR4>(call, pick_ns, grid);
+        case 32: return strip_launch_typed<K, Tin, Te, 32, SR32, SUMM>(call, pick_ns, grid);
+        case 16: return strip_launch_typed<K, Tin, Te, 16, SR16, SUMM>(call, pick_ns, grid);
+        case 8: return strip_launch_typed<K, Tin, Te, 8, SR8, SUMM>(call, pick_ns, grid);
+        default: return strip_launch_typed<K, Tin, Te, 4, SR4, SUMM>(call, pick_ns, grid);
     }
 }
 

@@ -193,8 +193,10 @@ def scan_summary(A: Tensor, B: Tensor, e0: Optional[Tensor]) -> tuple[Tensor, Te
         return e_last, A.new_ones(nb, hd, dtype=acc)
     e_last = torch.empty(nb, hd, dtype=acc, device=A.device)
     prod = torch.empty(nb, hd, dtype=acc, device=A.device)
+    ws = _workspace(nb, T, hd, A.dtype, 16, A.device)
     rc = _lib.lib().esa_scan_summary(A.data_ptr(), B.data_ptr(), nb, T, hd, dtype_code(A.dtype),
-                                     _ptr(e0c), e_last.data_ptr(), prod.data_ptr(), _stream(A))
+                                     _ptr(e0c), e_last.data_ptr(), prod.data_ptr(), ws.data_ptr(),
+                                     ws.numel(), _stream(A))
     _lib.check(rc, "esa_scan_summary")
     return e_last, prod
 

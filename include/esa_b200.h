@@ -124,14 +124,17 @@ int esa_scan_fwd_host(const void *A, const void *B, void *E, int64_t nb, int64_t
 
 /* Summary of a time slice: the per-channel end state E_{T-1} of the forward
  * recurrence (from e0, NULL: zero) and the product of A over [0, T), both in
- * the acc type, [nb, hd]; no per-step outputs (reads A and B once).  Two
+ * the acc type, [nb, hd]; no per-step outputs (reads A and B once).  The
+ * workspace (esa_scan_workspace_bytes, may be NULL) lets few-channel, long
+ * slices split their time axis across the GPU.  Two
  * consecutive slices compose as E_end = prod2 * E_end1 + E_end2 (from zero),
  * which is how GPUs holding consecutive time slices of one sequence combine
  * their carries.  Replaces nothing in the reference (it has no multi-device
  * path); part of the sequence-parallel scan built on thunder_scan
  * (esa/backends/thunder.py:70-159). */
 int esa_scan_summary(const void *A, const void *B, int64_t nb, int64_t T, int64_t hd, int dtype,
-                     const void *e0, void *e_last, void *prod, void *stream);
+                     const void *e0, void *e_last, void *prod, void *workspace,
+                     size_t workspace_bytes, void *stream);
 
 /* Reverse-time scan: the gradient of esa_scan_fwd.
  *   G_t = dE_t + A_{t+1} G_{t+1};  dB_t = G_t;  dA_t = G_t * E_{t-1}
