@@ -79,6 +79,14 @@ ESA_EXPORT int esa_scan_fwd_host(const void* A, const void* B, void* E, int64_t 
                          static_cast<cudaStream_t>(stream));
 }
 
+ESA_EXPORT int esa_scan_fwd_resume(const void* A, const void* B, void* E, int64_t nb, int64_t T,
+                                   int64_t hd, int dtype, int compass, const void* e0, void* e_last,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    return scan_fwd(A, B, E, nb, T, hd, dtype, compass, e0, e_last, workspace, workspace_bytes,
+                    static_cast<cudaStream_t>(stream), true);
+}
+
 ESA_EXPORT int esa_scan_summary(const void* A, const void* B, int64_t nb, int64_t T, int64_t hd,
                                 int dtype, const void* e0, void* e_last, void* prod, void* workspace,
                                 size_t workspace_bytes, void* stream) {

@@ -74,6 +74,9 @@ struct ScanCall {
     // multiple of 64), processed as independent rows of the strip scan
     int64_t npiece = 1, plen = 0;
     bool summ = false;  // summary pass: end state and coefficient product, no outputs
+    // split scans: the workspace already holds this problem's piece summaries
+    // (from a summary call on the same inputs): skip the summary pass
+    bool resume = false;
 };
 
 // Channel-strip scan (no inter-CTA waits).  Sets *taken = false when the
@@ -86,7 +89,8 @@ int sequential_scan_launch(const ScanCall& c);
 size_t lookback_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int compass);
 
 int scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd, int dtype,
-             int compass, const void* e0, void* e_last, void* ws, size_t ws_bytes, cudaStream_t s);
+             int compass, const void* e0, void* e_last, void* ws, size_t ws_bytes, cudaStream_t s,
+             bool resume = false);
 int scan_rev(const void* A, const void* E, const void* dE, void* dA, void* dB, int64_t nb, int64_t T,
              int64_t hd, int dtype, int compass, const void* e0, void* de0, void* ws, size_t ws_bytes,
              cudaStream_t s);

@@ -338,20 +338,23 @@ int run_split(ScanCall& c, bool* done) {
     void* cin = ws + 2 * plane;
     const bool rev = c.kind == Kind::RevPlain || c.kind == Kind::RevGated;
 
-    // pass 1: summaries of every piece from a zero state
-    ScanCall c1 = c;
-    c1.npiece = sp.npiece;
-    c1.plen = sp.plen;
-    c1.summ = true;
-    c1.a.e0 = nullptr;
-    c1.a.cin = nullptr;
-    c1.a.e_last = endst;
-    c1.a.prod_out = prod;
-    c1.ws = nullptr;
-    c1.ws_bytes = 0;
-    bool taken = false;
-    if (int rc = strip_scan_launch(c1, &taken)) return rc;
-    if (!taken) return ESA_OK;
+    // pass 1: summaries of every piece from a zero state (already in the
+    // workspace when resuming after a summary call on the same inputs)
+    if (!c.resume) {
+        ScanCall c1 = c;
+        c1.npiece = sp.npiece;
+        c1.plen = sp.plen;
+        c1.summ = true;
+        c1.a.e0 = nullptr;
+        c1.a.cin = nullptr;
+        c1.a.e_last = endst;
+        c1.a.prod_out = prod;
+        c1.ws = nullptr;
+        c1.ws_bytes = 0;
+        bool taken = false;
+        if (int rc = strip_scan_launch(c1, &taken)) return rc;
+        if (!taken) return ESA_OK;
+    }
     // pass 2: incoming states in time order
     const int64_t n = c.a.nb * c.a.hd;
     const int threads = 256;
@@ -382,9 +385,9 @@ int run_split(ScanCall& c, bool* done) {
     c3.a.e_last = nullptr;
     c3.ws = nullptr;
     c3.ws_bytes = 0;
-    taken = false;
-    if (int rc = strip_scan_launch(c3, &taken)) return rc;
-    if (!taken) return set_error(ESA_ERR_CUDA, "split scan: output pass not launched");
+    bool taken3 = false;
+    if (int rc = strip_scan_launch(c3, &taken3)) return rc;
+    if (!taken3) return set_error(ESA_ERR_CUDA, "split scan: output pass not launched");
     return ESA_OK;
 }
 
@@ -398,7 +401,8 @@ size_t scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int 
 }
 
 int scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd, int dtype,
-             int compass, const void* e0, void* e_last, void* ws, size_t ws_bytes, cudaStream_t s) {
+             int compass, const void* e0, void* e_last, void* ws, size_t ws_bytes, cudaStream_t s,
+             bool resume) {
     if (int rc = check_dims(nb, T, hd, compass)) return rc;
     const int es = dtype_size(dtype);
     if (es == 0) return set_error(ESA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code " + std::to_string(dtype));
@@ -419,6 +423,7 @@ int scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64
     c.ws_bytes = ws_bytes;
     c.stream = s;
     c.bulk_ok = rows_aligned(A, hd, hd, es) && rows_aligned(B, hd, hd, es) && rows_aligned(E, hd, hd, es);
+    c.resume = resume;
     return run(c);
 }
 

@@ -41,6 +41,7 @@ SIGNATURES = {
     "esa_scan_fwd_noalloc": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp]),
     "esa_scan_host_staging_bytes": (_sz, [_i64, _i64, _i64, _int, _int]),
     "esa_scan_fwd_host": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _sz, _vp]),
+    "esa_scan_fwd_resume": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _sz, _vp]),
     "esa_scan_summary": (_int, [_vp, _vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _vp, _sz, _vp]),
     "esa_scan_rev": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp,
                             _sz, _vp]),

@@ -13,9 +13,11 @@ slices only through one state per channel, so the exchange is tiny:
   4. scan (local): the slice's outputs from its exact incoming state C_r.
 
 Every rank reads A and B twice and writes E once (5 bytes-per-element passes
-against the 3 of a single-GPU scan); no wait spans more than the one
-all-gather.  Forward only: the reference has no multi-device path at all, and
-its training (esa/model.py) runs one sequence per GPU.
+against the 3 of a single-GPU scan; a few-channel slice's scan resumes from
+the piece summaries its summary call left in the shared workspace); no wait
+spans more than the one all-gather.  Forward only: the reference has no
+multi-device path at all, and its training (esa/model.py) runs one sequence
+per GPU.
 """
 
 from __future__ import annotations
@@ -25,7 +27,7 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _lib, ops
 
 
 def compose_carries(summaries: list[torch.Tensor], rank: int,
@@ -47,16 +49,40 @@ def sequence_parallel_scan(A: torch.Tensor, B: torch.Tensor, *, group=None, comp
     A, B: this rank's slice [B, T_r, H, D] (CUDA).  e0: the state before the
     first slice ([B, H, D] or [B, H*D]), used by every rank (only rank 0's
     carry starts from it).  Returns the slice of E in A's dtype.
+
+    The summary and the scan share one workspace: a few-channel slice is
+    summarised in time pieces (``esa_scan_summary``) and the scan resumes from
+    those piece summaries (``esa_scan_fwd_resume``), so each rank reads A and B
+    twice and writes E once.
     """
     if A.shape != B.shape or A.dim() != 4:
         raise ValueError(f"A and B must be the same [B,T,H,D], got {tuple(A.shape)} and {tuple(B.shape)}")
+    if not A.is_cuda or not B.is_cuda:
+        raise RuntimeError("sequence_parallel_scan needs CUDA tensors (no CPU fallback)")
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    nb, _, H, D = A.shape
-    e_end, prod = ops.scan_summary(A, B, None)
+    A = A.contiguous()
+    B = B.to(A.dtype).contiguous()
+    nb, T, H, D = A.shape
+    hd = H * D
+    acc = ops.acc_dtype(A.dtype)
+    code = ops.dtype_code(A.dtype)
+    L = _lib.lib()
+    stream = torch.cuda.current_stream(A.device).cuda_stream
+    ws = ops._workspace(nb, T, hd, A.dtype, int(compass), A.device)
+    e_end = torch.zeros(nb, hd, dtype=acc, device=A.device)
+    prod = torch.ones(nb, hd, dtype=acc, device=A.device)
+    if T > 0 and hd > 0 and nb > 0:
+        _lib.check(L.esa_scan_summary(A.data_ptr(), B.data_ptr(), nb, T, hd, code, None,
+                                      e_end.data_ptr(), prod.data_ptr(), ws.data_ptr(), ws.numel(),
+                                      stream), "esa_scan_summary")
     mine = torch.stack([e_end, prod])
     gathered = [torch.empty_like(mine) for _ in range(world)]
     dist.all_gather(gathered, mine, group=group)
-    carry = compose_carries(gathered, rank, e0)
-    E, _ = ops.scan(A, B, carry, int(compass))
+    carry = compose_carries(gathered, rank, e0).contiguous()
+    E = torch.empty_like(A)
+    if T > 0 and hd > 0 and nb > 0:
+        _lib.check(L.esa_scan_fwd_resume(A.data_ptr(), B.data_ptr(), E.data_ptr(), nb, T, hd, code,
+                                         int(compass), carry.data_ptr(), None, ws.data_ptr(),
+                                         ws.numel(), stream), "esa_scan_fwd_resume")
     return E

@@ -136,6 +136,18 @@ int esa_scan_summary(const void *A, const void *B, int64_t nb, int64_t T, int64_
                      const void *e0, void *e_last, void *prod, void *workspace,
                      size_t workspace_bytes, void *stream);
 
+/* esa_scan_fwd of a slice whose summary esa_scan_summary has just computed,
+ * with the same A, B, shape, dtype and workspace (and no other call using the
+ * workspace in between).  Few-channel, long slices are scanned in time pieces
+ * whose summaries the summary call left in the workspace; this call reuses
+ * them, so the pair reads A and B twice in all (summary + scan) instead of
+ * three times.  Other problems are scanned in full, as by esa_scan_fwd.  The
+ * results are those of esa_scan_fwd on the same arguments.  No counterpart in
+ * the reference: the second half of the sequence-parallel scan. */
+int esa_scan_fwd_resume(const void *A, const void *B, void *E, int64_t nb, int64_t T, int64_t hd,
+                        int dtype, int compass, const void *e0, void *e_last, void *workspace,
+                        size_t workspace_bytes, void *stream);
+
 /* Reverse-time scan: the gradient of esa_scan_fwd.
  *   G_t = dE_t + A_{t+1} G_{t+1};  dB_t = G_t;  dA_t = G_t * E_{t-1}
  * with E_{-1} = e0 (NULL: zero); de0 (nullable) receives A_0 * G_0, the

@@ -24,7 +24,7 @@ def test_header_declares_the_abi():
         "esa_abi_version", "esa_last_error", "esa_device_status", "esa_scan_workspace_bytes",
         "esa_scan_fwd", "esa_scan_rev", "esa_gated_scan_fwd", "esa_gated_scan_bwd",
         "esa_lightning_step", "esa_scan_fwd_noalloc", "esa_scan_summary",
-        "esa_scan_host_staging_bytes", "esa_scan_fwd_host"}
+        "esa_scan_host_staging_bytes", "esa_scan_fwd_host", "esa_scan_fwd_resume"}
 
 
 def test_library_loads_and_exports_every_declared_symbol():

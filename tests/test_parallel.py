@@ -164,3 +164,37 @@ def test_sequence_parallel_scan_nccl():
     ref = oracle.scan_fwd(A.double(), B.double())
     full = np.concatenate([got[r] for r in range(world)], axis=1)
     assert np.linalg.norm(full - ref) / np.linalg.norm(ref) < 1e-5
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(4, 16384, 32, 64), (2, 300, 4, 64)])
+def test_summary_then_resume_equals_full_scan(shape):
+    """esa_scan_fwd_resume after esa_scan_summary on the same workspace gives
+    the bits of esa_scan_fwd (split slices reuse the piece summaries; short
+    slices are scanned in full)."""
+    from esa import _lib, ops
+    torch.manual_seed(2)
+    A = torch.sigmoid(torch.randn(shape, device="cuda") + 3).to(torch.bfloat16)
+    B = (torch.randn(shape, device="cuda") * 0.5).to(torch.bfloat16)
+    nb, T, H, D = shape
+    hd = H * D
+    e0 = torch.randn(nb, hd, device="cuda")
+    ref, ref_last = ops.scan(A, B, e0, 16)
+    L = _lib.lib()
+    code = ops.dtype_code(A.dtype)
+    ws = ops._workspace(nb, T, hd, A.dtype, 16, A.device)
+    s = torch.cuda.current_stream().cuda_stream
+    e_end = torch.empty(nb, hd, device="cuda")
+    prod = torch.empty(nb, hd, device="cuda")
+    _lib.check(L.esa_scan_summary(A.data_ptr(), B.data_ptr(), nb, T, hd, code, None, e_end.data_ptr(),
+                                  prod.data_ptr(), ws.data_ptr(), ws.numel(), s), "summary")
+    E = torch.empty_like(A)
+    e_last = torch.empty(nb, hd, device="cuda")
+    _lib.check(L.esa_scan_fwd_resume(A.data_ptr(), B.data_ptr(), E.data_ptr(), nb, T, hd, code, 16,
+                                     e0.data_ptr(), e_last.data_ptr(), ws.data_ptr(), ws.numel(), s),
+               "resume")
+    torch.cuda.synchronize()
+    assert torch.equal(E, ref)
+    assert torch.equal(e_last, ref_last)
+    # the slice summary composes with e0 into the end state
+    torch.testing.assert_close(prod * e0 + e_end, e_last, rtol=1e-4, atol=1e-5)
