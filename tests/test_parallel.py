@@ -194,7 +194,14 @@ def test_summary_then_resume_equals_full_scan(shape):
                                      e0.data_ptr(), e_last.data_ptr(), ws.data_ptr(), ws.numel(), s),
                "resume")
     torch.cuda.synchronize()
-    assert torch.equal(E, ref)
-    assert torch.equal(e_last, ref_last)
+    if T >= 8192:
+        # split slice: the same deterministic passes, the same bits
+        assert torch.equal(E, ref)
+        assert torch.equal(e_last, ref_last)
+    else:
+        # scanned in full by the time-parallel kernel, whose association
+        # order may differ from call to call
+        torch.testing.assert_close(E.float(), ref.float(), rtol=1e-2, atol=1e-2)
+        torch.testing.assert_close(e_last, ref_last, rtol=1e-5, atol=1e-5)
     # the slice summary composes with e0 into the end state
     torch.testing.assert_close(prod * e0 + e_end, e_last, rtol=1e-4, atol=1e-5)
