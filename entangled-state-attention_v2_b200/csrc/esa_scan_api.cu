@@ -14,6 +14,7 @@
 //      one thread per channel, sequential over time.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -255,13 +256,23 @@ struct SplitPlan {
 // strip-pieces (eight waves of 2 CTAs on 148 SMs, so the last wave's
 // imbalance is small) with pieces of at least 1024 steps, a multiple of 64
 // steps (every strip tile length divides 64).
+int split_env(const char* name, int dflt) {
+    const char* v = getenv(name);
+    const int x = v ? atoi(v) : 0;
+    return x > 0 ? x : dflt;
+}
+
 SplitPlan split_plan(int64_t nb, int64_t T, int64_t hd, int wide_es) {
+    // tuning overrides, read once: ESA_SPLIT_MIN_T, ESA_SPLIT_TARGET, ESA_SPLIT_MIN_PIECE
+    static const int min_t = split_env("ESA_SPLIT_MIN_T", 8192);
+    static const int target = split_env("ESA_SPLIT_TARGET", 2400);
+    static const int min_piece = split_env("ESA_SPLIT_MIN_PIECE", 1024);
     SplitPlan p;
-    if (wide_es <= 0 || T < 8192) return p;
+    if (wide_es <= 0 || T < min_t) return p;
     const int64_t ws16 = 16 * (16 / wide_es);
     const int64_t strips16 = nb * ((hd + ws16 - 1) / ws16);
     if (strips16 <= 0 || strips16 >= 148) return p;
-    int64_t n = (2400 + strips16 - 1) / strips16;
+    int64_t n = (target + strips16 - 1) / strips16;
     // within 1/8 of that, the piece count whose strip-pieces fill whole waves
     // of 296 (2 CTAs on 148 SMs) best
     {
@@ -278,7 +289,7 @@ SplitPlan split_plan(int64_t nb, int64_t T, int64_t hd, int wide_es) {
         }
         n = best_n;
     }
-    if (n > T / 1024) n = T / 1024;
+    if (n > T / min_piece) n = T / min_piece;
     if (n < 2) return p;
     const int64_t plen = ((T + n - 1) / n + 63) / 64 * 64;
     p.npiece = (T + plen - 1) / plen;
