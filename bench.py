@@ -309,7 +309,7 @@ def run_ours(args) -> None:
                "h2d_bytes_per_step": 2 * N * 2, "d2h_bytes_per_step": N * 2,
                "ms_per_step": ms, "spot_check_rel_err": e2e_err,
                "api": "esa.backends.thunder.thunder_scan_host (C ABI esa_scan_fwd_host), "
-                      "pinned host buffers, copies pipelined in 8 MB chunks"}
+                      "pinned host buffers, copies pipelined in 32 MB chunks"}
         del hA, hB, hE
 
         # secondary figures: reverse scan fp16 and forward fp32 (kernel-only)

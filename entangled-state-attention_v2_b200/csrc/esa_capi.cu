@@ -46,6 +46,11 @@ ESA_EXPORT int esa_abi_version(void) { return ESA_ABI_VERSION; }
 
 ESA_EXPORT const char* esa_last_error(void) { return t_last_error.c_str(); }
 
+ESA_EXPORT int esa_wait_selftest(unsigned int* completed, unsigned int* waited_ms, void* stream) {
+    clear_error();
+    return wait_selftest(completed, waited_ms, static_cast<cudaStream_t>(stream));
+}
+
 ESA_EXPORT int esa_device_status(int device, int clear, unsigned int* status) {
     clear_error();
     if (status == nullptr) return set_error(ESA_ERR_INVALID_ARGUMENT, "status pointer is null");

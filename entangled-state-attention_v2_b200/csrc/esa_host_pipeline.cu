@@ -1,11 +1,12 @@
 // esa_host_pipeline.cu -- forward scan of HOST-resident A, B into host E,
 // with the host<->device copies pipelined against the scan.
 //
-// The tensor is cut into contiguous chunks (whole batch rows when a row is
-// small, else time pieces of one row, chained through the acc-type end state
-// e_last -> e0).  Chunk i goes through three queues:
+// The tensor is cut into contiguous chunks of about 32 MB per array (whole
+// batch rows when a row is small, else time pieces of one row, chained
+// through the acc-type end state e_last -> e0).  Chunk i goes through three
+// queues:
 //
-//   copy-in stream : A_i, B_i host -> staging slot (i mod kSlots)
+//   copy-in stream : A_i, B_i host -> staging slot (i mod the slot count)
 //   caller stream  : scan of slot i (esa_scan_fwd on the device copies)
 //   copy-out stream: E_i staging slot -> host
 //
@@ -18,6 +19,7 @@
 // allocates nothing: the staging slots, the scan workspace and the chunk
 // carries live in the caller's `staging` buffer.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -27,8 +29,25 @@
 namespace esa {
 namespace {
 
-constexpr int kSlots = 3;
-constexpr int64_t kChunkBytes = 8ll << 20;  // per array per chunk (target)
+constexpr int kMaxSlots = 8;
+
+int env_int(const char* name, int dflt, int lo, int hi) {
+    const char* v = getenv(name);
+    const int x = v ? atoi(v) : 0;
+    return (x >= lo && x <= hi) ? x : dflt;
+}
+// staging slots and chunk size per array (tuning overrides ESA_HOST_SLOTS,
+// ESA_HOST_CHUNK_MB, read once)
+int slots() {
+    static const int s = env_int("ESA_HOST_SLOTS", 3, 2, kMaxSlots);
+    return s;
+}
+int64_t chunk_bytes() {
+    // 32 MB: measured 70 GB/s end to end on [32,4096,16,64] fp16 against 65 at
+    // 8 MB (per-copy overheads); more slots than 3 gained nothing
+    static const int64_t b = (int64_t)env_int("ESA_HOST_CHUNK_MB", 32, 1, 256) << 20;
+    return b;
+}
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -46,15 +65,16 @@ struct Plan {
 Plan make_plan(int64_t nb, int64_t T, int64_t hd, int es, int compass) {
     Plan p{};
     const int64_t row_bytes = T * hd * es;
-    if (row_bytes <= kChunkBytes) {
-        p.rows_per_chunk = row_bytes > 0 ? std::max<int64_t>(1, kChunkBytes / row_bytes) : 1;
+    const int64_t chunk = chunk_bytes();
+    if (row_bytes <= chunk) {
+        p.rows_per_chunk = row_bytes > 0 ? std::max<int64_t>(1, chunk / row_bytes) : 1;
         p.rows_per_chunk = std::min<int64_t>(p.rows_per_chunk, std::max<int64_t>(nb, 1));
         p.steps_per_chunk = T;
         p.pieces_per_row = 1;
         p.nchunks = (nb + p.rows_per_chunk - 1) / p.rows_per_chunk;
     } else {
         p.rows_per_chunk = 1;
-        p.steps_per_chunk = std::max<int64_t>(1, kChunkBytes / (hd * es));
+        p.steps_per_chunk = std::max<int64_t>(1, chunk / (hd * es));
         p.pieces_per_row = (T + p.steps_per_chunk - 1) / p.steps_per_chunk;
         p.nchunks = nb * p.pieces_per_row;
     }
@@ -62,7 +82,7 @@ Plan make_plan(int64_t nb, int64_t T, int64_t hd, int es, int compass) {
     p.slot_array_bytes = round_up(size_t(p.rows_per_chunk) * p.steps_per_chunk * hd * es, 256);
     p.ws_bytes = round_up(scan_workspace_bytes(p.rows_per_chunk, p.steps_per_chunk, hd, es, compass), 256);
     p.carry_bytes = round_up(size_t(hd) * acc_es, 256);
-    p.total = size_t(kSlots) * 3 * p.slot_array_bytes + p.ws_bytes + 2 * p.carry_bytes;
+    p.total = size_t(slots()) * 3 * p.slot_array_bytes + p.ws_bytes + 2 * p.carry_bytes;
     return p;
 }
 
@@ -71,7 +91,7 @@ struct DeviceQueues {
     bool ready = false;
     cudaStream_t in = nullptr, out = nullptr;
     cudaEvent_t start = nullptr, end = nullptr;
-    cudaEvent_t loaded[kSlots], scanned[kSlots], stored[kSlots];
+    cudaEvent_t loaded[kMaxSlots], scanned[kMaxSlots], stored[kMaxSlots];
 };
 
 std::mutex g_mu;
@@ -85,7 +105,7 @@ int queues_for(int dev, DeviceQueues** q) {
                   cudaStreamCreateWithFlags(&d.out, cudaStreamNonBlocking) == cudaSuccess &&
                   cudaEventCreateWithFlags(&d.start, cudaEventDisableTiming) == cudaSuccess &&
                   cudaEventCreateWithFlags(&d.end, cudaEventDisableTiming) == cudaSuccess;
-        for (int k = 0; ok && k < kSlots; ++k)
+        for (int k = 0; ok && k < kMaxSlots; ++k)
             ok = cudaEventCreateWithFlags(&d.loaded[k], cudaEventDisableTiming) == cudaSuccess &&
                  cudaEventCreateWithFlags(&d.scanned[k], cudaEventDisableTiming) == cudaSuccess &&
                  cudaEventCreateWithFlags(&d.stored[k], cudaEventDisableTiming) == cudaSuccess;
@@ -123,11 +143,12 @@ int scan_fwd_host(const void* A, const void* B, void* E, int64_t nb, int64_t T, 
     DeviceQueues* q = nullptr;
     if (int rc = queues_for(dev, &q)) return rc;
 
+    const int nslot = slots();
     char* base = static_cast<char*>(staging);
-    char* slot[kSlots][3];
-    for (int k = 0; k < kSlots; ++k)
+    char* slot[kMaxSlots][3];
+    for (int k = 0; k < nslot; ++k)
         for (int a = 0; a < 3; ++a) slot[k][a] = base + (size_t(k) * 3 + a) * p.slot_array_bytes;
-    char* ws = base + size_t(kSlots) * 3 * p.slot_array_bytes;
+    char* ws = base + size_t(nslot) * 3 * p.slot_array_bytes;
     char* carry[2] = {ws + p.ws_bytes, ws + p.ws_bytes + p.carry_bytes};
 
     const char* hA = static_cast<const char*>(A);
@@ -146,7 +167,7 @@ int scan_fwd_host(const void* A, const void* B, void* E, int64_t nb, int64_t T, 
     cuda_ok(cudaStreamWaitEvent(q->out, q->start, 0), "cudaStreamWaitEvent");
 
     for (int64_t i = 0; i < p.nchunks && rc == ESA_OK; ++i) {
-        const int k = int(i % kSlots);
+        const int k = int(i % nslot);
         int64_t r0, nr, t0, nt;
         if (p.pieces_per_row == 1) {
             r0 = i * p.rows_per_chunk;
@@ -161,14 +182,14 @@ int scan_fwd_host(const void* A, const void* B, void* E, int64_t nb, int64_t T, 
         }
         const size_t off = size_t((r0 * T + t0) * hd) * es;
         const size_t bytes = size_t(nr * nt * hd) * es;
-        // copy in, once the scan of chunk i - kSlots has finished reading the slot
-        if (i >= kSlots) cuda_ok(cudaStreamWaitEvent(q->in, q->scanned[k], 0), "cudaStreamWaitEvent");
+        // copy in, once the scan of chunk i - nslot has finished reading the slot
+        if (i >= nslot) cuda_ok(cudaStreamWaitEvent(q->in, q->scanned[k], 0), "cudaStreamWaitEvent");
         cuda_ok(cudaMemcpyAsync(slot[k][0], hA + off, bytes, cudaMemcpyHostToDevice, q->in), "copy of A");
         cuda_ok(cudaMemcpyAsync(slot[k][1], hB + off, bytes, cudaMemcpyHostToDevice, q->in), "copy of B");
         cuda_ok(cudaEventRecord(q->loaded[k], q->in), "cudaEventRecord");
-        // scan, once the inputs are in and E of chunk i - kSlots has left the slot
+        // scan, once the inputs are in and E of chunk i - nslot has left the slot
         cuda_ok(cudaStreamWaitEvent(s, q->loaded[k], 0), "cudaStreamWaitEvent");
-        if (i >= kSlots) cuda_ok(cudaStreamWaitEvent(s, q->stored[k], 0), "cudaStreamWaitEvent");
+        if (i >= nslot) cuda_ok(cudaStreamWaitEvent(s, q->stored[k], 0), "cudaStreamWaitEvent");
         if (rc != ESA_OK) break;
         const int64_t piece = p.pieces_per_row == 1 ? 0 : i % p.pieces_per_row;
         const void* e0 = piece > 0 ? carry[(piece - 1) & 1] : nullptr;

@@ -109,6 +109,7 @@ size_t scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int 
 size_t scan_host_staging_bytes(int64_t nb, int64_t T, int64_t hd, int es, int compass);
 int scan_fwd_host(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd, int dtype,
                   int compass, void* staging, size_t staging_bytes, cudaStream_t s);
+int wait_selftest(unsigned* completed, unsigned* waited_ms, cudaStream_t s);
 int lightning_step(const void* qgv, int64_t qrs, int qdt, const void* state, void* new_state,
                    int sdt, void* z, int zdt, int64_t nb, int64_t C, double gmin, double gmax,
                    double eps, cudaStream_t s);

@@ -54,6 +54,14 @@ extern "C" {
 
 #define ESA_ABI_VERSION 1
 
+/* Diagnostic: runs the kernels' bounded mbarrier wait on a barrier that never
+ * completes, on `stream`, and synchronises it.  The wait gives up after its
+ * one-second budget: *completed = 0, *waited_ms = the time waited, and
+ * ESA_STATUS_COPY_TIMEOUT is set in the device status word (clear it with
+ * esa_device_status).  Lets a test check the timeout path without a fault or
+ * a hang.  No reference counterpart. */
+int esa_wait_selftest(unsigned int *completed, unsigned int *waited_ms, void *stream);
+
 /* Version of this ABI (ESA_ABI_VERSION). */
 int esa_abi_version(void);
 
@@ -103,14 +111,14 @@ int esa_scan_fwd_noalloc(const void *A, const void *B, void *E, int64_t nb, int6
                          int dtype, int compass, const void *e0, void *e_last, void *stream);
 
 /* Staging size (bytes) of esa_scan_fwd_host for this problem; 0 for invalid
- * arguments.  Bounded (about 80 MB) whatever the problem size. */
+ * arguments.  Bounded (about 300 MB) whatever the problem size. */
 size_t esa_scan_host_staging_bytes(int64_t nb, int64_t T, int64_t hd, int dtype, int compass);
 
 /* esa_scan_fwd on HOST buffers: A, B and E are host pointers ([nb, T, hd] of
  * `dtype`, page-locked for the copies to overlap; pageable memory works but
  * serialises), `staging` a 256-byte aligned device buffer of at least
  * esa_scan_host_staging_bytes().  The tensor moves through the device in
- * chunks of about 8 MB per array (whole rows, or time pieces of one row
+ * chunks of about 32 MB per array (whole rows, or time pieces of one row
  * chained through their end state): the host-to-device copy of one chunk, the
  * scan of the previous one (on `stream`) and the device-to-host copy of the
  * one before run concurrently on the two copy engines and the SMs.  Ordered

@@ -24,7 +24,8 @@ def test_header_declares_the_abi():
         "esa_abi_version", "esa_last_error", "esa_device_status", "esa_scan_workspace_bytes",
         "esa_scan_fwd", "esa_scan_rev", "esa_gated_scan_fwd", "esa_gated_scan_bwd",
         "esa_lightning_step", "esa_scan_fwd_noalloc", "esa_scan_summary",
-        "esa_scan_host_staging_bytes", "esa_scan_fwd_host", "esa_scan_fwd_resume"}
+        "esa_scan_host_staging_bytes", "esa_scan_fwd_host", "esa_scan_fwd_resume",
+        "esa_wait_selftest"}
 
 
 def test_library_loads_and_exports_every_declared_symbol():
@@ -54,7 +55,7 @@ def test_host_staging_is_bounded():
     big = L.esa_scan_host_staging_bytes(32, 4096, 1024, _lib.DTYPE_F16, 16)
     huge = L.esa_scan_host_staging_bytes(4, 262144, 2048, _lib.DTYPE_BF16, 16)
     assert 0 < small <= big
-    assert big < 128 << 20 and huge < 128 << 20
+    assert big < 512 << 20 and huge < 512 << 20
     assert L.esa_scan_host_staging_bytes(2, 64, 128, 9, 16) == 0
     rc = L.esa_scan_fwd_host(None, None, None, 1, 4, 8, _lib.DTYPE_F32, 16, None, 0, None)
     assert rc == -1 and "null host pointer" in _lib.last_error()
