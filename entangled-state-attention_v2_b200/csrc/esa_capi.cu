@@ -46,6 +46,26 @@ ESA_EXPORT int esa_abi_version(void) { return ESA_ABI_VERSION; }
 
 ESA_EXPORT const char* esa_last_error(void) { return t_last_error.c_str(); }
 
+ESA_EXPORT int esa_readout_fwd(const void* q, int64_t q_row_stride, int q_dtype, const void* E,
+                               int64_t e_row_stride, int e_dtype, void* y, int64_t y_row_stride,
+                               int y_dtype, void* rstd, int64_t rows, int64_t C, double eps,
+                               void* stream) {
+    clear_error();
+    return readout_fwd(q, q_row_stride, q_dtype, E, e_row_stride, e_dtype, y, y_row_stride, y_dtype, rstd,
+                       rows, C, eps, static_cast<cudaStream_t>(stream));
+}
+
+ESA_EXPORT int esa_readout_bwd(const void* dy, int64_t dy_row_stride, int dy_dtype, const void* q,
+                               int64_t q_row_stride, int q_dtype, const void* E, int64_t e_row_stride,
+                               int e_dtype, const void* rstd, void* dq, int64_t dq_row_stride,
+                               int dq_dtype, void* dE, int64_t de_row_stride, int de_dtype, int64_t rows,
+                               int64_t C, double eps, void* stream) {
+    clear_error();
+    return readout_bwd(dy, dy_row_stride, dy_dtype, q, q_row_stride, q_dtype, E, e_row_stride, e_dtype, rstd,
+                       dq, dq_row_stride, dq_dtype, dE, de_row_stride, de_dtype, rows, C, eps,
+                       static_cast<cudaStream_t>(stream));
+}
+
 ESA_EXPORT int esa_wait_selftest(unsigned int* completed, unsigned int* waited_ms, void* stream) {
     clear_error();
     return wait_selftest(completed, waited_ms, static_cast<cudaStream_t>(stream));

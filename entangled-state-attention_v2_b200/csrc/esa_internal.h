@@ -110,6 +110,11 @@ size_t scan_host_staging_bytes(int64_t nb, int64_t T, int64_t hd, int es, int co
 int scan_fwd_host(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd, int dtype,
                   int compass, void* staging, size_t staging_bytes, cudaStream_t s);
 int wait_selftest(unsigned* completed, unsigned* waited_ms, cudaStream_t s);
+int readout_fwd(const void* q, int64_t qrs, int qdt, const void* E, int64_t ers, int edt, void* y,
+                int64_t yrs, int ydt, void* rstd, int64_t rows, int64_t C, double eps, cudaStream_t s);
+int readout_bwd(const void* dy, int64_t dyrs, int dydt, const void* q, int64_t qrs, int qdt, const void* E,
+                int64_t ers, int edt, const void* rstd, void* dq, int64_t dqrs, int dqdt, void* dE,
+                int64_t ders, int dedt, int64_t rows, int64_t C, double eps, cudaStream_t s);
 int lightning_step(const void* qgv, int64_t qrs, int qdt, const void* state, void* new_state,
                    int sdt, void* z, int zdt, int64_t nb, int64_t C, double gmin, double gmax,
                    double eps, cudaStream_t s);

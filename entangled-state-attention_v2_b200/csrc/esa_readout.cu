@@ -1,0 +1,323 @@
+// esa_readout.cu -- the ESA layer readout, fused: forward and backward.
+//
+//   n = E * rsqrt(mean_C(E^2) + eps),   y = sigmoid(q) * n
+//
+// (the reference's `sigmoid(q) * E * rsqrt(E.pow(2).mean(-1) + eps)`,
+// esa/backends/thunder.py:304-311, esa/generation.py:270-293), one warp per
+// row of C channels: a pass for the sum of squares (warp-shuffle reduction),
+// a pass for the outputs; the row's rsqrt is kept for the backward.  The
+// backward of the same row:
+//
+//   dq = dy * n * s * (1 - s),   dn = dy * s,   s = sigmoid(q)
+//   dE = r * (dn - n * mean_C(dn * n)),   r = rsqrt(mean_C(E^2) + eps)
+//
+// Arithmetic in fp32 (fp64 when any operand is fp64) with one rounding per
+// output.  q, dq may be row-strided views (the q slice of the qgv projection
+// and of its gradient, row stride 3C); every operand has its own element type.
+// Roofline: HBM -- forward reads q and E and writes y (plus 4 bytes a row);
+// backward reads dy, q, E and writes dq and dE.
+#include <string>
+
+#include "../../include/esa_b200.h"
+#include "esa_internal.h"
+#include "esa_scan_common.cuh"
+
+namespace esa {
+namespace {
+
+// ---- element access by runtime dtype code ----------------------------------
+template <typename A>
+__device__ __forceinline__ A load1(const char* p, int dt) {
+    switch (dt) {
+        case ESA_DTYPE_F16: return A(__half2float(*reinterpret_cast<const __half*>(p)));
+        case ESA_DTYPE_BF16: return A(__bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(p)));
+        case ESA_DTYPE_F32: return A(*reinterpret_cast<const float*>(p));
+        default: return A(*reinterpret_cast<const double*>(p));
+    }
+}
+
+template <typename A>
+__device__ __forceinline__ void store1(char* p, int dt, A x) {
+    switch (dt) {
+        case ESA_DTYPE_F16: *reinterpret_cast<__half*>(p) = __float2half_rn(float(x)); break;
+        case ESA_DTYPE_BF16: *reinterpret_cast<__nv_bfloat16*>(p) = __float2bfloat16_rn(float(x)); break;
+        case ESA_DTYPE_F32: *reinterpret_cast<float*>(p) = float(x); break;
+        default: *reinterpret_cast<double*>(p) = double(x); break;
+    }
+}
+
+// 8 consecutive elements at p (16-byte aligned), widened to A
+template <typename A>
+__device__ __forceinline__ void load8(const char* p, int dt, A (&x)[8]) {
+    if (dt == ESA_DTYPE_F16 || dt == ESA_DTYPE_BF16) {
+        const uint4 v = *reinterpret_cast<const uint4*>(p);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float2 f;
+            if (dt == ESA_DTYPE_F16)
+                f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            else
+                f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+            x[2 * i] = A(f.x);
+            x[2 * i + 1] = A(f.y);
+        }
+    } else if (dt == ESA_DTYPE_F32) {
+        const float4 a = reinterpret_cast<const float4*>(p)[0];
+        const float4 b = reinterpret_cast<const float4*>(p)[1];
+        x[0] = A(a.x), x[1] = A(a.y), x[2] = A(a.z), x[3] = A(a.w);
+        x[4] = A(b.x), x[5] = A(b.y), x[6] = A(b.z), x[7] = A(b.w);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const double2 d = reinterpret_cast<const double2*>(p)[i];
+            x[2 * i] = A(d.x);
+            x[2 * i + 1] = A(d.y);
+        }
+    }
+}
+
+// 8 consecutive elements to p (16-byte aligned), rounded to the element type
+template <typename A>
+__device__ __forceinline__ void store8(char* p, int dt, const A (&x)[8]) {
+    if (dt == ESA_DTYPE_F16 || dt == ESA_DTYPE_BF16) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (dt == ESA_DTYPE_F16) {
+                const __half2 h = __floats2half2_rn(float(x[2 * i]), float(x[2 * i + 1]));
+                w[i] = *reinterpret_cast<const uint32_t*>(&h);
+            } else {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(float(x[2 * i]), float(x[2 * i + 1]));
+                w[i] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+        }
+        *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else if (dt == ESA_DTYPE_F32) {
+        reinterpret_cast<float4*>(p)[0] = make_float4(float(x[0]), float(x[1]), float(x[2]), float(x[3]));
+        reinterpret_cast<float4*>(p)[1] = make_float4(float(x[4]), float(x[5]), float(x[6]), float(x[7]));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            reinterpret_cast<double2*>(p)[i] = make_double2(double(x[2 * i]), double(x[2 * i + 1]));
+    }
+}
+
+// 8 elements of one row at channel c0: vector access, or element by element
+// (rows whose length or alignment the 16-byte path cannot take)
+template <typename A, bool VECT>
+__device__ __forceinline__ void row_load(const char* row, int dt, int es, int64_t c0, int64_t C, A (&x)[8]) {
+    if constexpr (VECT) {
+        load8(row + c0 * es, dt, x);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = (c0 + i < C) ? load1<A>(row + (c0 + i) * es, dt) : A(0);
+    }
+}
+
+template <typename A, bool VECT>
+__device__ __forceinline__ void row_store(char* row, int dt, int es, int64_t c0, int64_t C, const A (&x)[8]) {
+    if constexpr (VECT) {
+        store8(row + c0 * es, dt, x);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (c0 + i < C) store1<A>(row + (c0 + i) * es, dt, x[i]);
+    }
+}
+
+template <typename A>
+__device__ __forceinline__ A warp_sum(A x) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    return x;
+}
+
+__device__ __forceinline__ float rsqrt_acc(float x) { return 1.0f / sqrtf(x); }
+__device__ __forceinline__ double rsqrt_acc(double x) { return 1.0 / sqrt(x); }
+
+// One operand: base, row stride (elements), element type code and size.
+struct Opnd {
+    const char* p;
+    int64_t rs;
+    int dt, es;
+};
+struct MutOpnd {
+    char* p;
+    int64_t rs;
+    int dt, es;
+};
+
+struct ReadoutArgs {
+    Opnd q, E, dy;
+    MutOpnd y, dq, dE;
+    void* rstd;  // acc [rows]
+    int64_t rows, C;
+    double eps;
+};
+
+constexpr int kReadoutWarps = 8;
+
+template <typename A, bool VECT>
+__global__ void __launch_bounds__(32 * kReadoutWarps) readout_fwd_kernel(const ReadoutArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * kReadoutWarps;
+    const A inv_c = A(1) / A(a.C), eps = A(a.eps);
+    for (int64_t row = (int64_t)blockIdx.x * kReadoutWarps + (threadIdx.x >> 5); row < a.rows; row += nw) {
+        const char* er = a.E.p + row * a.E.rs * a.E.es;
+        const char* qr = a.q.p + row * a.q.rs * a.q.es;
+        char* yr = a.y.p + row * a.y.rs * a.y.es;
+        A ss = A(0);
+        for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
+            A e[8];
+            row_load<A, VECT>(er, a.E.dt, a.E.es, c0, a.C, e);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ss = fma_rn(e[i], e[i], ss);
+        }
+        const A r = rsqrt_acc(warp_sum(ss) * inv_c + eps);
+        for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
+            A e[8], q[8], y[8];
+            row_load<A, VECT>(er, a.E.dt, a.E.es, c0, a.C, e);
+            row_load<A, VECT>(qr, a.q.dt, a.q.es, c0, a.C, q);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = sigmoid_(q[i]) * (e[i] * r);
+            row_store<A, VECT>(yr, a.y.dt, a.y.es, c0, a.C, y);
+        }
+        if (lane == 0) static_cast<A*>(a.rstd)[row] = r;
+    }
+}
+
+template <typename A, bool VECT>
+__global__ void __launch_bounds__(32 * kReadoutWarps) readout_bwd_kernel(const ReadoutArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * kReadoutWarps;
+    const A inv_c = A(1) / A(a.C);
+    for (int64_t row = (int64_t)blockIdx.x * kReadoutWarps + (threadIdx.x >> 5); row < a.rows; row += nw) {
+        const char* er = a.E.p + row * a.E.rs * a.E.es;
+        const char* qr = a.q.p + row * a.q.rs * a.q.es;
+        const char* dyr = a.dy.p + row * a.dy.rs * a.dy.es;
+        char* dqr = a.dq.p + row * a.dq.rs * a.dq.es;
+        char* der = a.dE.p + row * a.dE.rs * a.dE.es;
+        const A r = static_cast<const A*>(a.rstd)[row];
+        // sum over the row of dn * n, dn = dy * s
+        A dot = A(0);
+        for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
+            A e[8], q[8], dy[8];
+            row_load<A, VECT>(er, a.E.dt, a.E.es, c0, a.C, e);
+            row_load<A, VECT>(qr, a.q.dt, a.q.es, c0, a.C, q);
+            row_load<A, VECT>(dyr, a.dy.dt, a.dy.es, c0, a.C, dy);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dot = fma_rn(dy[i] * sigmoid_(q[i]), e[i] * r, dot);
+        }
+        const A mdot = warp_sum(dot) * inv_c;
+        for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
+            A e[8], q[8], dy[8], dq[8], de[8];
+            row_load<A, VECT>(er, a.E.dt, a.E.es, c0, a.C, e);
+            row_load<A, VECT>(qr, a.q.dt, a.q.es, c0, a.C, q);
+            row_load<A, VECT>(dyr, a.dy.dt, a.dy.es, c0, a.C, dy);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const A s = sigmoid_(q[i]);
+                const A n = e[i] * r;
+                const A dn = dy[i] * s;
+                dq[i] = dy[i] * n * s * (A(1) - s);
+                de[i] = r * (dn - n * mdot);
+            }
+            row_store<A, VECT>(dqr, a.dq.dt, a.dq.es, c0, a.C, dq);
+            row_store<A, VECT>(der, a.dE.dt, a.dE.es, c0, a.C, de);
+        }
+    }
+}
+
+bool vec_ok(const void* p, int64_t rs, int es) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && (rs * es) % 16 == 0;
+}
+
+template <template <typename, bool> class Launch>
+int readout_launch(const ReadoutArgs& a, bool wide, bool vect, cudaStream_t s) {
+    const int64_t blocks_needed = (a.rows + kReadoutWarps - 1) / kReadoutWarps;
+    const int grid = (int)(blocks_needed < 148 * 16 ? blocks_needed : 148 * 16);
+    if (wide)
+        vect ? Launch<double, true>::go(a, grid, s) : Launch<double, false>::go(a, grid, s);
+    else
+        vect ? Launch<float, true>::go(a, grid, s) : Launch<float, false>::go(a, grid, s);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("readout launch: ") + cudaGetErrorString(e));
+    return ESA_OK;
+}
+
+template <typename A, bool V>
+struct FwdLaunch {
+    static void go(const ReadoutArgs& a, int grid, cudaStream_t s) {
+        readout_fwd_kernel<A, V><<<grid, 32 * kReadoutWarps, 0, s>>>(a);
+    }
+};
+template <typename A, bool V>
+struct BwdLaunch {
+    static void go(const ReadoutArgs& a, int grid, cudaStream_t s) {
+        readout_bwd_kernel<A, V><<<grid, 32 * kReadoutWarps, 0, s>>>(a);
+    }
+};
+
+int check_operand(const void* p, int64_t rs, int dt, int64_t C, const char* name, int* es) {
+    *es = dtype_size(dt);
+    if (*es == 0) return set_error(ESA_ERR_UNSUPPORTED_DTYPE, std::string(name) + ": unsupported dtype code");
+    if (p == nullptr) return set_error(ESA_ERR_INVALID_ARGUMENT, std::string(name) + " is null");
+    if (rs < C) return set_error(ESA_ERR_INVALID_ARGUMENT, std::string(name) + ": row stride smaller than C");
+    return ESA_OK;
+}
+
+}  // namespace
+
+int readout_fwd(const void* q, int64_t qrs, int qdt, const void* E, int64_t ers, int edt, void* y,
+                int64_t yrs, int ydt, void* rstd, int64_t rows, int64_t C, double eps, cudaStream_t s) {
+    if (rows < 0 || C < 0) return set_error(ESA_ERR_INVALID_ARGUMENT, "negative dimension");
+    if (rows == 0 || C == 0) return ESA_OK;
+    ReadoutArgs a{};
+    int es = 0;
+    if (int rc = check_operand(q, qrs, qdt, C, "q", &es)) return rc;
+    a.q = {static_cast<const char*>(q), qrs, qdt, es};
+    if (int rc = check_operand(E, ers, edt, C, "E", &es)) return rc;
+    a.E = {static_cast<const char*>(E), ers, edt, es};
+    if (int rc = check_operand(y, yrs, ydt, C, "y", &es)) return rc;
+    a.y = {static_cast<char*>(y), yrs, ydt, es};
+    if (rstd == nullptr) return set_error(ESA_ERR_INVALID_ARGUMENT, "rstd is null");
+    a.rstd = rstd;
+    a.rows = rows;
+    a.C = C;
+    a.eps = eps;
+    const bool wide = qdt == ESA_DTYPE_F64 || edt == ESA_DTYPE_F64 || ydt == ESA_DTYPE_F64;
+    const bool vect = C % 8 == 0 && vec_ok(q, qrs, a.q.es) && vec_ok(E, ers, a.E.es) && vec_ok(y, yrs, a.y.es);
+    return readout_launch<FwdLaunch>(a, wide, vect, s);
+}
+
+int readout_bwd(const void* dy, int64_t dyrs, int dydt, const void* q, int64_t qrs, int qdt, const void* E,
+                int64_t ers, int edt, const void* rstd, void* dq, int64_t dqrs, int dqdt, void* dE,
+                int64_t ders, int dedt, int64_t rows, int64_t C, double eps, cudaStream_t s) {
+    if (rows < 0 || C < 0) return set_error(ESA_ERR_INVALID_ARGUMENT, "negative dimension");
+    if (rows == 0 || C == 0) return ESA_OK;
+    ReadoutArgs a{};
+    int es = 0;
+    if (int rc = check_operand(dy, dyrs, dydt, C, "dy", &es)) return rc;
+    a.dy = {static_cast<const char*>(dy), dyrs, dydt, es};
+    if (int rc = check_operand(q, qrs, qdt, C, "q", &es)) return rc;
+    a.q = {static_cast<const char*>(q), qrs, qdt, es};
+    if (int rc = check_operand(E, ers, edt, C, "E", &es)) return rc;
+    a.E = {static_cast<const char*>(E), ers, edt, es};
+    if (int rc = check_operand(dq, dqrs, dqdt, C, "dq", &es)) return rc;
+    a.dq = {static_cast<char*>(dq), dqrs, dqdt, es};
+    if (int rc = check_operand(dE, ders, dedt, C, "dE", &es)) return rc;
+    a.dE = {static_cast<char*>(dE), ders, dedt, es};
+    if (rstd == nullptr) return set_error(ESA_ERR_INVALID_ARGUMENT, "rstd is null");
+    a.rstd = const_cast<void*>(rstd);
+    a.rows = rows;
+    a.C = C;
+    a.eps = eps;
+    const bool wide = dydt == ESA_DTYPE_F64 || qdt == ESA_DTYPE_F64 || edt == ESA_DTYPE_F64 ||
+                      dqdt == ESA_DTYPE_F64 || dedt == ESA_DTYPE_F64;
+    const bool vect = C % 8 == 0 && vec_ok(dy, dyrs, a.dy.es) && vec_ok(q, qrs, a.q.es) &&
+                      vec_ok(E, ers, a.E.es) && vec_ok(dq, dqrs, a.dq.es) && vec_ok(dE, ders, a.dE.es);
+    return readout_launch<BwdLaunch>(a, wide, vect, s);
+}
+
+}  // namespace esa

@@ -36,6 +36,10 @@ SIGNATURES = {
     "esa_abi_version": (_int, []),
     "esa_last_error": (ctypes.c_char_p, []),
     "esa_device_status": (_int, [_int, _int, ctypes.POINTER(ctypes.c_uint)]),
+    "esa_readout_fwd": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _i64,
+                               _f64, _vp]),
+    "esa_readout_bwd": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _int, _vp, _vp, _i64,
+                               _int, _vp, _i64, _int, _i64, _i64, _f64, _vp]),
     "esa_wait_selftest": (_int, [ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_uint), _vp]),
     "esa_scan_workspace_bytes": (_sz, [_i64, _i64, _i64, _int, _int]),
     "esa_scan_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _sz, _vp]),

@@ -9,8 +9,14 @@ esa/backends/flare.py:198-225):
     E = scan(A.to(scan_dtype), B.to(scan_dtype))                  -- kernel a (+ b backward)
     y = out_proj( (sigmoid(q) * E * rsqrt(mean_C(E^2) + eps)).to(x.dtype) )
 
-The gate prologue and its chain rule run inside the scan kernels
-(``esa_b200::gated_scan``), so A and B are never materialised in HBM.
+Everything between the qgv projection and out_proj is one op
+(``esa_b200::layer_core``): the gated scan with the gate prologue fused, then
+the fused readout kernel; its backward is the fused readout backward (which
+writes the q third of d qgv and dE) and the gated reverse scan with the gate
+chain rule (which writes the g and v thirds), so neither A, B nor the readout
+intermediates are materialised and d qgv needs no concatenation.  Under
+autocast the readout writes y directly in the autocast dtype that out_proj
+would cast it to (the same value: rounding the fp32 result once).
 """
 
 from __future__ import annotations
@@ -29,8 +35,13 @@ def require_cuda_input(x: torch.Tensor, who: str) -> None:
 
 
 def readout(q: torch.Tensor, E: torch.Tensor, eps: float, out_dtype: torch.dtype) -> torch.Tensor:
-    """sigmoid(q) * E * rsqrt(mean(E^2) + eps) over the channel axis, in E's
-    dtype, cast to out_dtype (thunder.py:304-311, generation.py:270-293)."""
+    """sigmoid(q) * E * rsqrt(mean(E^2) + eps) over the channel axis, cast to
+    out_dtype (thunder.py:304-311, generation.py:270-293).  Without autograd:
+    the fused readout kernel (fp32 arithmetic, one rounding); when a gradient
+    is needed: the same math in torch ops, in E's dtype."""
+    if (not torch.is_grad_enabled() or not (q.requires_grad or E.requires_grad)) and q.is_cuda \
+            and E.is_cuda and q.dim() == E.dim() == 3:
+        return ops.readout(q, E, eps, out_dtype)
     q = q.to(E.dtype)
     E = E * torch.rsqrt(E.pow(2).mean(dim=-1, keepdim=True) + eps)
     return (torch.sigmoid(q) * E).to(out_dtype)
@@ -42,10 +53,11 @@ def gated_layer_forward(layer, x: torch.Tensor, scan_dtype: torch.dtype | None, 
     require_cuda_input(x, who)
     B, T, C = x.shape
     qgv = layer.qgv(x)
-    q, gate_raw, value_raw = qgv.split(C, dim=-1)
     if scan_dtype is None:
         scan_dtype = qgv.dtype
-    E, _ = ops.gated_scan(gate_raw, value_raw, None, float(layer.gate_min),
-                          float(layer.gate_max), int(compass), scan_dtype)
-    y = readout(q, E, float(layer.eps), x.dtype)
+    out_dtype = x.dtype
+    if torch.is_autocast_enabled("cuda"):
+        out_dtype = torch.get_autocast_dtype("cuda")
+    y, _, _ = ops.layer_core(qgv, float(layer.gate_min), float(layer.gate_max), float(layer.eps),
+                             int(compass), scan_dtype, out_dtype)
     return layer.dropout(layer.out_proj(y))

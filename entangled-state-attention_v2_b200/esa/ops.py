@@ -364,3 +364,125 @@ def check_device_status(device=None) -> None:
             names.append("bulk copy wait ran out")
         raise RuntimeError(f"ESA kernel on cuda:{idx} reported: {', '.join(names)} "
                            f"(status {st:#x}); results of the affected launch are invalid")
+
+
+# --------------------------------------------------------------------------
+# Layer core: qgv -> y (gated scan + fused readout) and its backward, which
+# writes the whole qgv gradient in place (ThunderESA.forward between the qgv
+# projection and out_proj, esa/backends/thunder.py:282-311)
+# --------------------------------------------------------------------------
+def _core_views(qgv: Tensor) -> tuple[Tensor, int, int, int]:
+    if qgv.dim() != 3 or qgv.shape[-1] % 3 != 0:
+        raise ValueError(f"qgv must be [B,T,3C], got {tuple(qgv.shape)}")
+    nb, T, C3 = qgv.shape
+    return qgv.contiguous(), nb, T, C3 // 3
+
+
+@torch.library.custom_op("esa_b200::layer_core", mutates_args=())
+def layer_core(qgv: Tensor, gate_min: float, gate_max: float, eps: float, compass: int,
+               scan_dtype: torch.dtype, out_dtype: torch.dtype) -> tuple[Tensor, Tensor, Tensor]:
+    """(y, E, rstd): E = gated scan of the g, v slices of qgv [B,T,3C] in
+    scan_dtype, y = sigmoid(q) * E * rsqrt(mean_C(E^2) + eps) in out_dtype,
+    rstd the per-row rsqrt (kept for the backward)."""
+    _require_cuda("esa layer core", qgv)
+    qgv, nb, T, C = _core_views(qgv)
+    L = _lib.lib()
+    es = qgv.element_size()
+    rdt = dtype_code(qgv.dtype)
+    acc = acc_dtype(scan_dtype, qgv.dtype, out_dtype)
+    E = torch.empty(nb, T, C, dtype=scan_dtype, device=qgv.device)
+    y = torch.empty(nb, T, C, dtype=out_dtype, device=qgv.device)
+    rstd = torch.empty(nb * T, dtype=acc, device=qgv.device)
+    if nb * T * C == 0:
+        return y, E, rstd
+    base = qgv.data_ptr()
+    ws = _workspace(nb, T, C, _widest(qgv.dtype, scan_dtype), compass, qgv.device)
+    s = _stream(qgv)
+    _lib.check(L.esa_gated_scan_fwd(base + C * es, base + 2 * C * es, 3 * C, rdt, E.data_ptr(),
+                                    dtype_code(scan_dtype), nb, T, C, float(gate_min), float(gate_max),
+                                    1, int(compass), None, None, ws.data_ptr(), ws.numel(), s),
+               "esa_gated_scan_fwd")
+    _lib.check(L.esa_readout_fwd(base, 3 * C, rdt, E.data_ptr(), C, dtype_code(scan_dtype), y.data_ptr(),
+                                 C, dtype_code(out_dtype), rstd.data_ptr(), nb * T, C, float(eps), s),
+               "esa_readout_fwd")
+    return y, E, rstd
+
+
+@layer_core.register_fake
+def _(qgv, gate_min, gate_max, eps, compass, scan_dtype, out_dtype):
+    nb, T, C3 = qgv.shape
+    C = C3 // 3
+    return (qgv.new_empty(nb, T, C, dtype=out_dtype), qgv.new_empty(nb, T, C, dtype=scan_dtype),
+            qgv.new_empty(nb * T, dtype=acc_dtype(scan_dtype, qgv.dtype, out_dtype)))
+
+
+@torch.library.custom_op("esa_b200::layer_core_backward", mutates_args=())
+def layer_core_backward(dy: Tensor, qgv: Tensor, E: Tensor, rstd: Tensor, gate_min: float,
+                        gate_max: float, eps: float, compass: int) -> Tensor:
+    """d qgv [B,T,3C] (qgv's dtype): the readout backward writes the q third
+    and dE, the gated reverse scan the g and v thirds."""
+    _require_cuda("esa layer core backward", dy, qgv, E, rstd)
+    qgv, nb, T, C = _core_views(qgv)
+    dy = dy.contiguous()
+    E = E.contiguous()
+    L = _lib.lib()
+    es = qgv.element_size()
+    rdt = dtype_code(qgv.dtype)
+    edt = dtype_code(E.dtype)
+    dqgv = torch.empty_like(qgv)
+    if nb * T * C == 0:
+        return dqgv.zero_()
+    dE = torch.empty_like(E)
+    base, dbase = qgv.data_ptr(), dqgv.data_ptr()
+    s = _stream(qgv)
+    _lib.check(L.esa_readout_bwd(dy.data_ptr(), C, dtype_code(dy.dtype), base, 3 * C, rdt, E.data_ptr(), C,
+                                 edt, rstd.data_ptr(), dbase, 3 * C, rdt, dE.data_ptr(), C, edt, nb * T, C,
+                                 float(eps), s), "esa_readout_bwd")
+    ws = _workspace(nb, T, C, _widest(qgv.dtype, E.dtype), compass, qgv.device)
+    _lib.check(L.esa_gated_scan_bwd(base + C * es, base + 2 * C * es, 3 * C, rdt, E.data_ptr(), dE.data_ptr(),
+                                    edt, dbase + C * es, dbase + 2 * C * es, 3 * C, rdt, nb, T, C,
+                                    float(gate_min), float(gate_max), 1, int(compass), None, None,
+                                    ws.data_ptr(), ws.numel(), s), "esa_gated_scan_bwd")
+    return dqgv
+
+
+@layer_core_backward.register_fake
+def _(dy, qgv, E, rstd, gate_min, gate_max, eps, compass):
+    return torch.empty_like(qgv)
+
+
+def _core_setup(ctx, inputs, output):
+    qgv, gmin, gmax, eps, compass, scan_dtype, out_dtype = inputs
+    _, E, rstd = output
+    ctx.save_for_backward(qgv, E, rstd)
+    ctx.args = (gmin, gmax, eps, compass)
+
+
+def _core_bwd(ctx, dy, dE_unused, drstd_unused):
+    qgv, E, rstd = ctx.saved_tensors
+    gmin, gmax, eps, compass = ctx.args
+    if dy is None:
+        return None, None, None, None, None, None, None
+    dqgv = layer_core_backward(dy, qgv, E, rstd, gmin, gmax, eps, compass)
+    return dqgv, None, None, None, None, None, None
+
+
+torch.library.register_autograd("esa_b200::layer_core", _core_bwd, setup_context=_core_setup)
+
+
+def readout(q: Tensor, E: Tensor, eps: float, out_dtype: torch.dtype) -> Tensor:
+    """Fused readout sigmoid(q) * E * rsqrt(mean_C(E^2) + eps), [B,T,C] (q may
+    be a row-strided slice), no autograd (inference: prefill)."""
+    _require_cuda("esa readout", q, E)
+    nb, T, C = E.shape
+    E = E.contiguous()
+    qr, rs_q = _rows(q)
+    y = torch.empty(nb, T, C, dtype=out_dtype, device=E.device)
+    if nb * T * C == 0:
+        return y
+    rstd = torch.empty(nb * T, dtype=acc_dtype(q.dtype, E.dtype, out_dtype), device=E.device)
+    _lib.check(_lib.lib().esa_readout_fwd(qr.data_ptr(), rs_q, dtype_code(qr.dtype), E.data_ptr(), C,
+                                          dtype_code(E.dtype), y.data_ptr(), C, dtype_code(out_dtype),
+                                          rstd.data_ptr(), nb * T, C, float(eps), _stream(E)),
+               "esa_readout_fwd")
+    return y

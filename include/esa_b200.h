@@ -54,6 +54,29 @@ extern "C" {
 
 #define ESA_ABI_VERSION 1
 
+/* ESA readout of `rows` rows of C channels, fused:
+ *   y = sigmoid(q) * E * rsqrt(mean_C(E^2) + eps)
+ * in fp32 (fp64 if any operand is fp64), one rounding per output.  Every
+ * operand is a row-strided view of its own dtype (row strides in elements:
+ * e.g. 3*C for the q slice of a qgv [.., 3C] projection); rstd receives the
+ * per-row rsqrt ([rows], acc type) for esa_readout_bwd.  Replaces the readout
+ * of ThunderESA.forward (esa/backends/thunder.py:304-311) and `_readout`
+ * (esa/generation.py:270-293) up to the out_proj. */
+int esa_readout_fwd(const void *q, int64_t q_row_stride, int q_dtype, const void *E,
+                    int64_t e_row_stride, int e_dtype, void *y, int64_t y_row_stride, int y_dtype,
+                    void *rstd, int64_t rows, int64_t C, double eps, void *stream);
+
+/* Gradient of esa_readout_fwd: from dy, q, E and the forward's rstd,
+ *   dq = dy * n * s * (1 - s),  dE = r * (dy * s - n * mean_C(dy * s * n)),
+ * with s = sigmoid(q), r = rstd, n = E * r.  dq and dE are row-strided
+ * outputs of their own dtypes (dq can be the q slice of a qgv gradient).
+ * Replaces the autograd of the readout (esa/backends/thunder.py:304-311). */
+int esa_readout_bwd(const void *dy, int64_t dy_row_stride, int dy_dtype, const void *q,
+                    int64_t q_row_stride, int q_dtype, const void *E, int64_t e_row_stride,
+                    int e_dtype, const void *rstd, void *dq, int64_t dq_row_stride, int dq_dtype,
+                    void *dE, int64_t de_row_stride, int de_dtype, int64_t rows, int64_t C,
+                    double eps, void *stream);
+
 /* Diagnostic: runs the kernels' bounded mbarrier wait on a barrier that never
  * completes, on `stream`, and synchronises it.  The wait gives up after its
  * one-second budget: *completed = 0, *waited_ms = the time waited, and
