@@ -235,6 +235,12 @@ int run(ScanCall& c) {
     bool done = false;
     if (int rc = run_split(c, &done)) return rc;
     if (done) return ESA_OK;
+    // tuning override: ESA_SCAN_PATH=lookback skips the strip scan
+    static const bool force_lookback = [] {
+        const char* v = getenv("ESA_SCAN_PATH");
+        return v != nullptr && std::string(v) == "lookback";
+    }();
+    if (force_lookback && c.kind != Kind::FwdSummary) return lookback_scan_launch(c);
     bool taken = false;
     const int rc = strip_scan_launch(c, &taken);
     if (rc != ESA_OK || taken) return rc;
