@@ -66,6 +66,31 @@ ESA_EXPORT int esa_readout_bwd(const void* dy, int64_t dy_row_stride, int dy_dty
                        static_cast<cudaStream_t>(stream));
 }
 
+ESA_EXPORT int esa_layer_norm_fwd(const void* x, int x_dtype, const void* w, const void* b, int w_dtype,
+                                  void* y, int y_dtype, float* mean, float* rstd, int64_t rows, int64_t C,
+                                  double eps, void* stream) {
+    clear_error();
+    return layer_norm_fwd(x, x_dtype, w, b, w_dtype, y, y_dtype, mean, rstd, rows, C, eps,
+                          static_cast<cudaStream_t>(stream));
+}
+
+ESA_EXPORT size_t esa_layer_norm_workspace_bytes(int64_t rows, int64_t C) {
+    if (rows < 0 || C <= 0) return 0;
+    return (size_t)layer_norm_partial_rows(rows > 0 ? rows : 1) * 2 * (size_t)C * sizeof(float);
+}
+
+ESA_EXPORT int esa_layer_norm_bwd(const void* dy, int dy_dtype, const void* x, int x_dtype, const void* w,
+                                  int w_dtype, const float* mean, const float* rstd, void* dx, void* dw,
+                                  void* db, void* workspace, size_t workspace_bytes, int64_t rows, int64_t C,
+                                  void* stream) {
+    clear_error();
+    const size_t need = (size_t)layer_norm_partial_rows(rows > 0 ? rows : 1) * 2 * (size_t)(C > 0 ? C : 0) * sizeof(float);
+    if (workspace == nullptr || workspace_bytes < need)
+        return set_error(ESA_ERR_WORKSPACE, "layer norm backward: workspace smaller than esa_layer_norm_workspace_bytes()");
+    return layer_norm_bwd(dy, dy_dtype, x, x_dtype, w, w_dtype, mean, rstd, dx, dw, db,
+                          static_cast<float*>(workspace), rows, C, static_cast<cudaStream_t>(stream));
+}
+
 ESA_EXPORT int esa_wait_selftest(unsigned int* completed, unsigned int* waited_ms, void* stream) {
     clear_error();
     return wait_selftest(completed, waited_ms, static_cast<cudaStream_t>(stream));

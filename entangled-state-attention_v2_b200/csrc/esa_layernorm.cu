@@ -1,0 +1,287 @@
+// esa_layernorm.cu -- LayerNorm of the ESAModel residual stream, fused with
+// the dtype cast its consumer needs.
+//
+//   y = (x - mean) * rstd * w + b,   rstd = 1 / sqrt(var + eps)   (biased var)
+//
+// (the blocks' `F.layer_norm(x, (C,), w, b, 1e-5)`, esa/model.py of the
+// reference).  Under fp16/bf16 autocast PyTorch computes it in fp32, writes
+// an fp32 tensor, and the Linear that consumes it casts that to the autocast
+// dtype in a separate copy; here the normalisation writes the autocast dtype
+// directly (the same values: one rounding of the fp32 result), and the
+// backward takes the Linear's 16-bit input gradient without the cast back.
+//
+// Forward: one warp per row of C channels (mean, then the variance about it,
+// then the outputs; arithmetic in fp32); the row's mean and rstd are kept.
+// Backward, per row: xhat = (x - mean) rstd, g = dy w,
+//   dx = rstd (g - mean_C(g) - xhat mean_C(g xhat));
+// the column sums dw = sum_rows dy xhat, db = sum_rows dy are accumulated per
+// lane over the rows of a CTA, reduced across its warps in shared memory into
+// one partial row per CTA, and the partial rows are summed by a second kernel
+// in a fixed order (deterministic, no atomics).
+#include <string>
+
+#include "../../include/esa_b200.h"
+#include "esa_internal.h"
+#include "esa_rowops.cuh"
+
+namespace esa {
+namespace {
+
+using namespace rowops;
+
+constexpr int kLnWarps = 8;
+constexpr int kLnMaxChunks = 8;  // 8-channel chunks per lane: C <= 2048
+
+struct LnArgs {
+    const char* x;
+    int xdt, xes;
+    const char* w;
+    const char* b;
+    int wdt, wes;
+    char* y;
+    int ydt, yes;
+    const char* dy;
+    int dydt, dyes;
+    char* dx;
+    float* mean;
+    float* rstd;
+    float* partial;  // [grid][2][C]: dw, db partial sums per CTA
+    int64_t rows, C;
+    float eps;
+};
+
+__global__ void __launch_bounds__(32 * kLnWarps) ln_fwd_kernel(const LnArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * kLnWarps;
+    const float inv_c = 1.0f / float(a.C);
+    for (int64_t row = (int64_t)blockIdx.x * kLnWarps + (threadIdx.x >> 5); row < a.rows; row += nw) {
+        const char* xr = a.x + row * a.C * a.xes;
+        char* yr = a.y + row * a.C * a.yes;
+        float s = 0.f;
+        for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
+            float v[8];
+            load8(xr + c0 * a.xes, a.xdt, v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) s += v[i];
+        }
+        const float mu = warp_sum(s) * inv_c;
+        float q = 0.f;
+        for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
+            float v[8];
+            load8(xr + c0 * a.xes, a.xdt, v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float d = v[i] - mu;
+                q = fmaf(d, d, q);
+            }
+        }
+        const float r = rsqrt_acc(warp_sum(q) * inv_c + a.eps);
+        for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
+            float v[8], w[8], bb[8], o[8];
+            load8(xr + c0 * a.xes, a.xdt, v);
+            load8(a.w + c0 * a.wes, a.wdt, w);
+            load8(a.b + c0 * a.wes, a.wdt, bb);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = fmaf((v[i] - mu) * r, w[i], bb[i]);
+            store8(yr + c0 * a.yes, a.ydt, o);
+        }
+        if (lane == 0) {
+            a.mean[row] = mu;
+            a.rstd[row] = r;
+        }
+    }
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_kernel(const LnArgs a) {
+    extern __shared__ float ln_smem[];  // [kLnWarps][2][C]
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int64_t nw = (int64_t)gridDim.x * kLnWarps;
+    const float inv_c = 1.0f / float(a.C);
+    float dw[NCH][8], db[NCH][8];
+#pragma unroll
+    for (int k = 0; k < NCH; ++k)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dw[k][i] = db[k][i] = 0.f;
+    for (int64_t row = (int64_t)blockIdx.x * kLnWarps + warp; row < a.rows; row += nw) {
+        const char* xr = a.x + row * a.C * a.xes;
+        const char* dyr = a.dy + row * a.C * a.dyes;
+        char* dxr = a.dx + row * a.C * a.xes;
+        const float mu = a.mean[row], r = a.rstd[row];
+        float sg = 0.f, sgx = 0.f;
+#pragma unroll
+        for (int k = 0; k < NCH; ++k) {
+            const int64_t c0 = lane * 8 + k * 256;
+            if (c0 < a.C) {
+                float v[8], d[8], w[8];
+                load8(xr + c0 * a.xes, a.xdt, v);
+                load8(dyr + c0 * a.dyes, a.dydt, d);
+                load8(a.w + c0 * a.wes, a.wdt, w);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float xh = (v[i] - mu) * r;
+                    const float g = d[i] * w[i];
+                    sg += g;
+                    sgx = fmaf(g, xh, sgx);
+                    dw[k][i] = fmaf(d[i], xh, dw[k][i]);
+                    db[k][i] += d[i];
+                }
+            }
+        }
+        const float mg = warp_sum(sg) * inv_c, mgx = warp_sum(sgx) * inv_c;
+#pragma unroll
+        for (int k = 0; k < NCH; ++k) {
+            const int64_t c0 = lane * 8 + k * 256;
+            if (c0 < a.C) {
+                float v[8], d[8], w[8], o[8];
+                load8(xr + c0 * a.xes, a.xdt, v);
+                load8(dyr + c0 * a.dyes, a.dydt, d);
+                load8(a.w + c0 * a.wes, a.wdt, w);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float xh = (v[i] - mu) * r;
+                    o[i] = r * (d[i] * w[i] - mg - xh * mgx);
+                }
+                store8(dxr + c0 * a.xes, a.xdt, o);
+            }
+        }
+    }
+    // this CTA's column partial sums: warps through shared memory, in order
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+        const int64_t c0 = lane * 8 + k * 256;
+        if (c0 < a.C)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                ln_smem[(warp * 2 + 0) * a.C + c0 + i] = dw[k][i];
+                ln_smem[(warp * 2 + 1) * a.C + c0 + i] = db[k][i];
+            }
+    }
+    __syncthreads();
+    for (int64_t c = threadIdx.x; c < 2 * a.C; c += blockDim.x) {
+        const int which = (int)(c / a.C);
+        const int64_t ch = c - which * a.C;
+        float s = 0.f;
+        for (int w = 0; w < kLnWarps; ++w) s += ln_smem[(w * 2 + which) * a.C + ch];
+        a.partial[((int64_t)blockIdx.x * 2 + which) * a.C + ch] = s;
+    }
+}
+
+// dw, db = sums of the CTAs' partial rows, in CTA order
+__global__ void ln_bwd_finalize_kernel(const float* __restrict__ partial, int nblocks, int64_t C,
+                                       char* dw, char* db, int wdt, int wes) {
+    const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= 2 * C) return;
+    const int which = (int)(c / C);
+    const int64_t ch = c - which * C;
+    float s = 0.f;
+    for (int k = 0; k < nblocks; ++k) s += partial[((int64_t)k * 2 + which) * C + ch];
+    store1<float>((which == 0 ? dw : db) + ch * wes, wdt, s);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int ln_check(const void* p, int dt, int64_t C, const char* name, int* es) {
+    *es = dtype_size(dt);
+    if (*es == 0) return set_error(ESA_ERR_UNSUPPORTED_DTYPE, std::string(name) + ": unsupported dtype code");
+    if (p == nullptr) return set_error(ESA_ERR_INVALID_ARGUMENT, std::string(name) + " is null");
+    if (!aligned16(p) || (C * *es) % 16 != 0)
+        return set_error(ESA_ERR_INVALID_ARGUMENT, std::string(name) + ": rows must be 16-byte aligned");
+    return ESA_OK;
+}
+
+int ln_grid(int64_t rows) {
+    const int64_t need = (rows + kLnWarps - 1) / kLnWarps;
+    return (int)(need < 148 * 8 ? need : 148 * 8);
+}
+
+}  // namespace
+
+int layer_norm_partial_rows(int64_t rows) { return ln_grid(rows); }
+
+int layer_norm_fwd(const void* x, int xdt, const void* w, const void* b, int wdt, void* y, int ydt,
+                   float* mean, float* rstd, int64_t rows, int64_t C, double eps, cudaStream_t s) {
+    if (rows < 0 || C <= 0 || C % 8 != 0 || C > 256 * kLnMaxChunks)
+        return set_error(ESA_ERR_INVALID_ARGUMENT, "layer norm: C must be a positive multiple of 8, at most 2048");
+    if (rows == 0) return ESA_OK;
+    LnArgs a{};
+    if (int rc = ln_check(x, xdt, C, "x", &a.xes)) return rc;
+    if (int rc = ln_check(w, wdt, C, "w", &a.wes)) return rc;
+    if (int rc = ln_check(b, wdt, C, "b", &a.wes)) return rc;
+    if (int rc = ln_check(y, ydt, C, "y", &a.yes)) return rc;
+    if (!mean || !rstd) return set_error(ESA_ERR_INVALID_ARGUMENT, "layer norm: null mean/rstd");
+    a.x = static_cast<const char*>(x);
+    a.xdt = xdt;
+    a.w = static_cast<const char*>(w);
+    a.b = static_cast<const char*>(b);
+    a.wdt = wdt;
+    a.y = static_cast<char*>(y);
+    a.ydt = ydt;
+    a.mean = mean;
+    a.rstd = rstd;
+    a.rows = rows;
+    a.C = C;
+    a.eps = (float)eps;
+    ln_fwd_kernel<<<ln_grid(rows), 32 * kLnWarps, 0, s>>>(a);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("layer norm launch: ") + cudaGetErrorString(e));
+    return ESA_OK;
+}
+
+int layer_norm_bwd(const void* dy, int dydt, const void* x, int xdt, const void* w, int wdt,
+                   const float* mean, const float* rstd, void* dx, void* dw, void* db, float* partial,
+                   int64_t rows, int64_t C, cudaStream_t s) {
+    if (rows < 0 || C <= 0 || C % 8 != 0 || C > 256 * kLnMaxChunks)
+        return set_error(ESA_ERR_INVALID_ARGUMENT, "layer norm: C must be a positive multiple of 8, at most 2048");
+    LnArgs a{};
+    int es = 0;
+    if (int rc = ln_check(x, xdt, C, "x", &a.xes)) return rc;
+    if (int rc = ln_check(dx, xdt, C, "dx", &es)) return rc;
+    if (int rc = ln_check(w, wdt, C, "w", &a.wes)) return rc;
+    if (int rc = ln_check(dw, wdt, C, "dw", &es)) return rc;
+    if (int rc = ln_check(db, wdt, C, "db", &es)) return rc;
+    if (int rc = ln_check(dy, dydt, C, "dy", &a.dyes)) return rc;
+    if (!mean || !rstd || !partial) return set_error(ESA_ERR_INVALID_ARGUMENT, "layer norm: null buffer");
+    a.x = static_cast<const char*>(x);
+    a.xdt = xdt;
+    a.w = static_cast<const char*>(w);
+    a.wdt = wdt;
+    a.dy = static_cast<const char*>(dy);
+    a.dydt = dydt;
+    a.dx = static_cast<char*>(dx);
+    a.mean = const_cast<float*>(mean);
+    a.rstd = const_cast<float*>(rstd);
+    a.partial = partial;
+    a.rows = rows;
+    a.C = C;
+    const int grid = rows > 0 ? ln_grid(rows) : 1;
+    const size_t smem = (size_t)kLnWarps * 2 * C * sizeof(float);
+    const int nch = (int)((C + 255) / 256);
+    cudaError_t e = cudaSuccess;
+    auto launch = [&](auto kernel) {
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess) kernel<<<grid, 32 * kLnWarps, smem, s>>>(a);
+    };
+    switch (nch) {
+        case 1: launch(ln_bwd_kernel<1>); break;
+        case 2: launch(ln_bwd_kernel<2>); break;
+        case 3: launch(ln_bwd_kernel<3>); break;
+        case 4: launch(ln_bwd_kernel<4>); break;
+        case 5: launch(ln_bwd_kernel<5>); break;
+        case 6: launch(ln_bwd_kernel<6>); break;
+        case 7: launch(ln_bwd_kernel<7>); break;
+        default: launch(ln_bwd_kernel<8>); break;
+    }
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e == cudaSuccess) {
+        const int threads = 256;
+        ln_bwd_finalize_kernel<<<(unsigned)((2 * C + threads - 1) / threads), threads, 0, s>>>(
+            partial, grid, C, static_cast<char*>(dw), static_cast<char*>(db), wdt, a.wes);
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("layer norm backward: ") + cudaGetErrorString(e));
+    return ESA_OK;
+}
+
+}  // namespace esa

@@ -27,6 +27,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import ops
 from .generation import GenerationResult, GenerationStats, parse_engine_spec, sample_next_token
 from .layer import ESA
 
@@ -86,6 +87,16 @@ class _LayerNorm(nn.Module):
         self.bias = nn.Parameter(torch.zeros(ndim)) if bias else None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        # On the GPU: the fused kernel, writing the dtype the consuming Linear
+        # computes in (the autocast dtype under autocast; the same values as an
+        # fp32 result cast by the Linear).  Elsewhere (no bias, fp64, odd
+        # widths): F.layer_norm.
+        if ops.layer_norm_supported(x, self.weight, self.bias):
+            out_dtype = x.dtype
+            if torch.is_autocast_enabled("cuda"):
+                out_dtype = torch.get_autocast_dtype("cuda")
+            y, _, _ = ops.layer_norm(x, self.weight, self.bias, 1e-5, out_dtype)
+            return y
         return F.layer_norm(x, self.weight.shape, self.weight, self.bias, 1e-5)
 
 

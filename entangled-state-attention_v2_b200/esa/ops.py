@@ -486,3 +486,86 @@ def readout(q: Tensor, E: Tensor, eps: float, out_dtype: torch.dtype) -> Tensor:
                                           rstd.data_ptr(), nb * T, C, float(eps), _stream(E)),
                "esa_readout_fwd")
     return y
+
+
+# --------------------------------------------------------------------------
+# LayerNorm of the ESAModel residual stream, written in its consumer's dtype
+# (the blocks' F.layer_norm, esa/model.py)
+# --------------------------------------------------------------------------
+def layer_norm_supported(x: Tensor, weight: Tensor, bias: Optional[Tensor]) -> bool:
+    C = x.shape[-1]
+    ok_dt = (torch.float16, torch.bfloat16, torch.float32)
+    return (x.is_cuda and bias is not None and weight.is_cuda and C % 8 == 0 and 0 < C <= 2048
+            and x.dtype in ok_dt and weight.dtype in ok_dt and bias.dtype == weight.dtype)
+
+
+@torch.library.custom_op("esa_b200::layer_norm", mutates_args=())
+def layer_norm(x: Tensor, weight: Tensor, bias: Tensor, eps: float,
+               out_dtype: torch.dtype) -> tuple[Tensor, Tensor, Tensor]:
+    """(y, mean, rstd): y = (x - mean) rstd w + b over the last axis in
+    out_dtype (fp32 arithmetic); mean, rstd per row (fp32) for the backward."""
+    _require_cuda("esa layer norm", x, weight, bias)
+    C = x.shape[-1]
+    xc = x.contiguous()
+    rows = xc.numel() // C if C else 0
+    y = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    mean = torch.empty(rows, dtype=torch.float32, device=x.device)
+    rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+    if rows == 0:
+        return y, mean, rstd
+    _lib.check(_lib.lib().esa_layer_norm_fwd(xc.data_ptr(), dtype_code(xc.dtype), weight.contiguous().data_ptr(),
+                                             bias.contiguous().data_ptr(), dtype_code(weight.dtype), y.data_ptr(),
+                                             dtype_code(out_dtype), mean.data_ptr(), rstd.data_ptr(), rows, C,
+                                             float(eps), _stream(x)), "esa_layer_norm_fwd")
+    return y, mean, rstd
+
+
+@layer_norm.register_fake
+def _(x, weight, bias, eps, out_dtype):
+    rows = x.numel() // x.shape[-1] if x.shape[-1] else 0
+    return (x.new_empty(x.shape, dtype=out_dtype), x.new_empty(rows, dtype=torch.float32),
+            x.new_empty(rows, dtype=torch.float32))
+
+
+@torch.library.custom_op("esa_b200::layer_norm_backward", mutates_args=())
+def layer_norm_backward(dy: Tensor, x: Tensor, weight: Tensor, mean: Tensor,
+                        rstd: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    """(dx, dw, db) of esa_b200::layer_norm (dw, db reduced in a fixed order)."""
+    _require_cuda("esa layer norm backward", dy, x, weight, mean, rstd)
+    C = x.shape[-1]
+    xc = x.contiguous()
+    dyc = dy.contiguous()
+    rows = xc.numel() // C if C else 0
+    dx = torch.empty_like(xc)
+    dw = torch.empty_like(weight)
+    db = torch.empty_like(weight)
+    L = _lib.lib()
+    n = int(L.esa_layer_norm_workspace_bytes(rows, C))
+    ws = torch.empty(max(n // 4, 1), dtype=torch.float32, device=x.device)
+    _lib.check(L.esa_layer_norm_bwd(dyc.data_ptr(), dtype_code(dyc.dtype), xc.data_ptr(), dtype_code(xc.dtype),
+                                    weight.contiguous().data_ptr(), dtype_code(weight.dtype), mean.data_ptr(),
+                                    rstd.data_ptr(), dx.data_ptr(), dw.data_ptr(), db.data_ptr(), ws.data_ptr(),
+                                    ws.numel() * 4, rows, C, _stream(x)), "esa_layer_norm_bwd")
+    return dx, dw, db
+
+
+@layer_norm_backward.register_fake
+def _(dy, x, weight, mean, rstd):
+    return torch.empty_like(x), torch.empty_like(weight), torch.empty_like(weight)
+
+
+def _ln_setup(ctx, inputs, output):
+    x, weight, bias, eps, out_dtype = inputs
+    _, mean, rstd = output
+    ctx.save_for_backward(x, weight, mean, rstd)
+
+
+def _ln_bwd(ctx, dy, dmean_unused, drstd_unused):
+    x, weight, mean, rstd = ctx.saved_tensors
+    if dy is None:
+        return None, None, None, None, None
+    dx, dw, db = layer_norm_backward(dy, x, weight, mean, rstd)
+    return dx, dw, db, None, None
+
+
+torch.library.register_autograd("esa_b200::layer_norm", _ln_bwd, setup_context=_ln_setup)

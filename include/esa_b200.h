@@ -77,6 +77,28 @@ int esa_readout_bwd(const void *dy, int64_t dy_row_stride, int dy_dtype, const v
                     void *dE, int64_t de_row_stride, int de_dtype, int64_t rows, int64_t C,
                     double eps, void *stream);
 
+/* LayerNorm of `rows` contiguous rows of C channels (C a multiple of 8, at
+ * most 2048; 16-byte aligned rows):
+ *   y = (x - mean) / sqrt(var + eps) * w + b     (biased variance, fp32 math)
+ * x, w/b and y each of their own dtype; y is rounded once from the fp32
+ * result (e.g. straight to the autocast dtype the consuming Linear would cast
+ * an fp32 result to).  mean and rstd ([rows] fp32) are kept for the backward.
+ * Replaces the blocks' F.layer_norm (esa/model.py of the reference) in the
+ * ESAModel residual stream. */
+int esa_layer_norm_fwd(const void *x, int x_dtype, const void *w, const void *b, int w_dtype,
+                       void *y, int y_dtype, float *mean, float *rstd, int64_t rows, int64_t C,
+                       double eps, void *stream);
+
+/* Scratch (bytes) of esa_layer_norm_bwd: per-CTA partial column sums. */
+size_t esa_layer_norm_workspace_bytes(int64_t rows, int64_t C);
+
+/* Gradient of esa_layer_norm_fwd: dx (x's dtype), dw and db (w's dtype) from
+ * dy (own dtype), x, w and the forward's mean/rstd.  dw and db are reduced in a
+ * fixed order (deterministic). */
+int esa_layer_norm_bwd(const void *dy, int dy_dtype, const void *x, int x_dtype, const void *w,
+                       int w_dtype, const float *mean, const float *rstd, void *dx, void *dw, void *db,
+                       void *workspace, size_t workspace_bytes, int64_t rows, int64_t C, void *stream);
+
 /* Diagnostic: runs the kernels' bounded mbarrier wait on a barrier that never
  * completes, on `stream`, and synchronises it.  The wait gives up after its
  * one-second budget: *completed = 0, *waited_ms = the time waited, and
