@@ -168,16 +168,28 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_kernel(const LnArgs a) {
     }
 }
 
-// dw, db = sums of the CTAs' partial rows, in CTA order
-__global__ void ln_bwd_finalize_kernel(const float* __restrict__ partial, int nblocks, int64_t C,
-                                       char* dw, char* db, int wdt, int wes) {
-    const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= 2 * C) return;
-    const int which = (int)(c / C);
-    const int64_t ch = c - which * C;
+// dw, db = sums of the CTA partial rows: a block of 32 x 8 threads per 32
+// columns, each of the 8 thread rows summing every 8th partial row, then a
+// fixed-order sum of the 8 in shared memory (deterministic)
+__global__ void __launch_bounds__(256) ln_bwd_finalize_kernel(const float* __restrict__ partial, int nblocks,
+                                                              int64_t C, char* dw, char* db, int wdt, int wes) {
+    __shared__ float part[8][33];
+    const int64_t c = (int64_t)blockIdx.x * 32 + threadIdx.x;  // column of [2][C]
     float s = 0.f;
-    for (int k = 0; k < nblocks; ++k) s += partial[((int64_t)k * 2 + which) * C + ch];
-    store1<float>((which == 0 ? dw : db) + ch * wes, wdt, s);
+    if (c < 2 * C) {
+        const int which = (int)(c / C);
+        const int64_t ch = c - which * C;
+        for (int k = threadIdx.y; k < nblocks; k += 8) s += partial[((int64_t)k * 2 + which) * C + ch];
+    }
+    part[threadIdx.y][threadIdx.x] = s;
+    __syncthreads();
+    if (threadIdx.y == 0 && c < 2 * C) {
+        float tot = 0.f;
+        for (int y = 0; y < 8; ++y) tot += part[y][threadIdx.x];
+        const int which = (int)(c / C);
+        const int64_t ch = c - which * C;
+        store1<float>((which == 0 ? dw : db) + ch * wes, wdt, tot);
+    }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -196,9 +208,17 @@ int ln_grid(int64_t rows) {
     return (int)(need < 148 * 8 ? need : 148 * 8);
 }
 
+// backward: fewer CTAs (each reduces its rows' dw, db once, then writes one
+// partial row), two per SM (measured: 126 us on [32768, 768] against 141 us
+// with 8 per SM and 146 us with 4 per SM and the sums in shared memory)
+int ln_bwd_grid(int64_t rows) {
+    const int64_t need = (rows + kLnWarps - 1) / kLnWarps;
+    return (int)(need < 148 * 2 ? need : 148 * 2);
+}
+
 }  // namespace
 
-int layer_norm_partial_rows(int64_t rows) { return ln_grid(rows); }
+int layer_norm_partial_rows(int64_t rows) { return ln_bwd_grid(rows); }
 
 int layer_norm_fwd(const void* x, int xdt, const void* w, const void* b, int wdt, void* y, int ydt,
                    float* mean, float* rstd, int64_t rows, int64_t C, double eps, cudaStream_t s) {
@@ -255,7 +275,7 @@ int layer_norm_bwd(const void* dy, int dydt, const void* x, int xdt, const void*
     a.partial = partial;
     a.rows = rows;
     a.C = C;
-    const int grid = rows > 0 ? ln_grid(rows) : 1;
+    const int grid = rows > 0 ? ln_bwd_grid(rows) : 1;
     const size_t smem = (size_t)kLnWarps * 2 * C * sizeof(float);
     const int nch = (int)((C + 255) / 256);
     cudaError_t e = cudaSuccess;
@@ -275,8 +295,7 @@ int layer_norm_bwd(const void* dy, int dydt, const void* x, int xdt, const void*
     }
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e == cudaSuccess) {
-        const int threads = 256;
-        ln_bwd_finalize_kernel<<<(unsigned)((2 * C + threads - 1) / threads), threads, 0, s>>>(
+        ln_bwd_finalize_kernel<<<(unsigned)((2 * C + 31) / 32), dim3(32, 8), 0, s>>>(
             partial, grid, C, static_cast<char*>(dw), static_cast<char*>(db), wdt, a.wes);
         e = cudaGetLastError();
     }
