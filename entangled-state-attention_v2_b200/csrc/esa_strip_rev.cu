@@ -6,7 +6,7 @@
 #ifndef ESA_REV_SR4
 #define ESA_REV_SR4 1
 #define ESA_REV_SR8 2
-#define ESA_REV_SR16 4
+#define ESA_REV_SR16 2  // measured: 5.54 vs 5.45 TB/s on the [32,4096,16,64] fp16 reverse, no spill
 #define ESA_REV_SR32 2  // measured: 6.2 vs 5.8 TB/s on the [32,4096,16,64] fp32 reverse
 #endif
 
