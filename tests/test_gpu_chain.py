@@ -1,10 +1,13 @@
 """Parity of the scan on few-channel, long-time-axis problems.
 
 With few channels per batch row the strips cannot fill the GPU, so the time
-axis is split across CTAs (the time-parallel look-back scan: per-tile
-aggregates, a decoupled look-back over earlier tiles, outputs from the exact
-incoming state).  These shapes (2 to 8 strips' worth of channels, thousands of
-steps) exercise that split in every kind, with initial and final states.
+axis is cut across CTAs: below 8192 steps by the time-parallel look-back scan
+(per-tile aggregates, a decoupled look-back over earlier tiles, outputs from
+the exact incoming state), from 8192 steps by the split scan (time pieces as
+strip rows: summary pass, composition of the pieces' incoming states, output
+pass).  These shapes (a few strips' worth of channels, thousands of steps)
+exercise both in every kind, with initial and final states, and the host
+pipeline's time pieces.
 Same bar as the other scan tests: relative Frobenius error against the fp64
 oracle on the same rounded inputs -- 1e-5 fp32, 2e-3 fp16/bf16, 1e-12 fp64.
 """
@@ -129,3 +132,69 @@ def test_chained_long_sequence_properties():
     e_end, prod = ops.scan_summary(A, B, None)
     assert rel(e_last, e_end) < 1e-4
     del prod
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_split_reverse_with_states(dtype):
+    """T >= 8192 with few channels: the reverse scan runs split into time
+    pieces (summary pass, composition in descending time, output pass)."""
+    from esa import ops
+    shape = (2, 10000, 2, 64)
+    A, B, g = _inputs(shape, dtype, 14)
+    nb, T, H, D = shape
+    e0 = torch.randn(nb, H * D, generator=g, dtype=torch.float64).float()
+    Ad = A.to(DEV).requires_grad_(True)
+    Bd = B.to(DEV).requires_grad_(True)
+    e0d = e0.to(DEV).requires_grad_(True)
+    E, _ = ops.scan(Ad, Bd, e0d, 16)
+    dE = torch.randn(shape, generator=g, dtype=torch.float64).to(dtype)
+    E.backward(dE.to(DEV))
+    dA_ref, dB_ref, de0_ref = oracle.scan_rev(A.double(), E.detach().double().cpu(), dE.double(),
+                                              e0=e0.double())
+    assert rel(Bd.grad, dB_ref) < TOL[dtype]
+    assert rel(Ad.grad, dA_ref) < TOL[dtype]
+    assert rel(e0d.grad, de0_ref) < TOL[dtype]
+
+
+@pytest.mark.parametrize("raw_dtype,scan_dtype", [(torch.float32, torch.float32), (torch.float16, torch.float16)])
+def test_split_gated_fwd_bwd(raw_dtype, scan_dtype):
+    """Fused gated scans split into time pieces (T = 9000, 128 channels): the
+    summary passes run the gate prologue, the reverse one in descending time."""
+    from esa import ops
+    g = torch.Generator().manual_seed(15)
+    Bsz, T, C = 1, 9000, 128
+    qgv = torch.randn(Bsz, T, 3 * C, generator=g).to(raw_dtype)
+    gr, vr = qgv[..., C:2 * C], qgv[..., 2 * C:]
+    qd = qgv.to(DEV)
+    grd, vrd = qd[..., C:2 * C], qd[..., 2 * C:]
+    e0 = torch.randn(Bsz, C, generator=g).to(DEV)
+    E, e_last = ops.gated_scan(grd, vrd, e0, 0.8, 0.995, 16, scan_dtype)
+    A64, B64 = oracle.gate(gr, vr)
+    Ar = torch.from_numpy(A64).to(scan_dtype).double()
+    Br = torch.from_numpy(B64).to(scan_dtype).double()
+    ref = oracle.scan_fwd(Ar.reshape(Bsz, T, 1, C), Br.reshape(Bsz, T, 1, C),
+                          e0=e0.double().cpu().reshape(Bsz, 1, C)).reshape(Bsz, T, C)
+    tol = max(TOL[scan_dtype], TOL[raw_dtype])
+    assert rel(E, ref) < tol
+    assert rel(e_last, ref[:, -1]) < tol
+    dE = torch.randn(Bsz, T, C, generator=g).to(scan_dtype)
+    dg, dv, de0 = ops.gated_scan_backward(grd, vrd, E, dE.to(DEV), e0, 0.8, 0.995, 16)
+    dA, dB, de0_ref = oracle.scan_rev(Ar.reshape(Bsz, T, 1, C), E.double().cpu().reshape(Bsz, T, 1, C),
+                                      dE.double().reshape(Bsz, T, 1, C),
+                                      e0=e0.double().cpu().reshape(Bsz, 1, C))
+    dg_ref, dv_ref = oracle.gate_bwd(gr, vr, dA.reshape(Bsz, T, C), dB.reshape(Bsz, T, C))
+    assert rel(dg, dg_ref) < tol * 2
+    assert rel(dv, dv_ref) < tol * 2
+    assert rel(de0, de0_ref.reshape(Bsz, C)) < tol * 2
+
+
+def test_host_pipeline_time_pieces_with_split():
+    """A 72 MB row: the host pipeline cuts it into time pieces chained through
+    their end states, and each piece (65536 steps, 128 channels) is itself
+    scanned split."""
+    from esa.backends.thunder import thunder_scan_host
+    A, B, _ = _inputs((1, 140000, 2, 64), torch.float32, 16)
+    A, B = A.pin_memory(), B.pin_memory()
+    E = thunder_scan_host(A, B)
+    ref = oracle.scan_fwd(A.double(), B.double())
+    assert rel(E, ref) < TOL[torch.float32]
