@@ -255,18 +255,19 @@ struct SplitPlan {
     int64_t npiece = 1, plen = 0;
 };
 
-// Pieces per batch row for an [nb, T, hd] problem whose widest element has
-// `wide_es` bytes: split when 128-channel-wide strips (16 lanes) number fewer
-// than one per SM of a B200 and the time axis is long (>= 8192 steps; shorter
-// problems do better on the look-back scan, measured).  Aim at about 2400
-// strip-pieces (eight waves of 2 CTAs on 148 SMs, so the last wave's
-// imbalance is small) with pieces of at least 1024 steps, a multiple of 64
-// steps (every strip tile length divides 64).
 int split_env(const char* name, int dflt) {
     const char* v = getenv(name);
     const int x = v ? atoi(v) : 0;
     return x > 0 ? x : dflt;
 }
+
+// Pieces per batch row for an [nb, T, hd] problem whose widest element has
+// `wide_es` bytes: split when 128-channel-wide strips (16 lanes) number fewer
+// than one per SM of a B200 and the time axis is long (>= 8192 steps; shorter
+// problems measured faster unsplit: the extra summary pass does not pay).
+// Aim at about 2400 strip-pieces (eight waves of 2 CTAs on 148 SMs, so the
+// last wave's imbalance is small) with pieces of at least 1024 steps, a
+// multiple of 64 steps (every strip tile length divides 64).
 
 SplitPlan split_plan(int64_t nb, int64_t T, int64_t hd, int wide_es) {
     // tuning overrides, read once: ESA_SPLIT_MIN_T, ESA_SPLIT_TARGET, ESA_SPLIT_MIN_PIECE
