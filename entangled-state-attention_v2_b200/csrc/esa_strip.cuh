@@ -5,14 +5,20 @@
 // The recurrence state never leaves the chip between tiles, so there is no
 // inter-CTA communication and no waiting on other CTAs at all; the only waits
 // are on this CTA's own TMA copies.  Parallelism comes from the channel
-// count: nb*hd channels give nb*ceil(hd/WS) strips (e.g. 512 for the
-// [32, 4096, 16, 64] fp16 microbenchmark with 64-channel strips).
+// count: nb*hd channels give nb*ceil(hd/WS) strips (e.g. 256 for the
+// [32, 4096, 16, 64] fp16 microbenchmark with 128-channel strips).  For the
+// split scan (few channels, long T) every batch row is cut into time pieces
+// that are processed as rows of their own (StripParams::npiece/plen), from an
+// incoming state per piece (KArgs::cin); the SUMM instantiations write only
+// each piece's end state and coefficient product.
 //
 // Data movement.  One thread issues 3-D tiled TMA loads
 // (cp.async.bulk.tensor.3d, tensor map [nb, T, hd], box [1, LT, WS], L2
 // evict-first) of every staged array into an NSTAGE-deep ring of shared-memory
-// stages, completing on one mbarrier per stage; the CTA consumes stage j while
-// the next NSTAGE-1 tiles are in flight.  Outputs are stored from registers
+// stages (two by default), completing on one mbarrier per stage; the CTA
+// consumes stage j while the next NSTAGE-1 tiles are in flight, and at the end
+// of a strip the freed stages already take the first tiles of the CTA's next
+// strip.  Outputs are stored from registers
 // with 16-byte coalesced stores.  Each input byte crosses HBM once, each
 // output byte once: the kernel's DRAM traffic is exactly the algorithmic one.
 //
