@@ -70,8 +70,19 @@ ESA_EXPORT int esa_layer_norm_fwd(const void* x, int x_dtype, const void* w, con
                                   void* y, int y_dtype, float* mean, float* rstd, int64_t rows, int64_t C,
                                   double eps, void* stream) {
     clear_error();
-    return layer_norm_fwd(x, x_dtype, w, b, w_dtype, y, y_dtype, mean, rstd, rows, C, eps,
+    return layer_norm_fwd(x, x_dtype, nullptr, 0, nullptr, w, b, w_dtype, y, y_dtype, mean, rstd, rows, C, eps,
                           static_cast<cudaStream_t>(stream));
+}
+
+ESA_EXPORT int esa_add_layer_norm_fwd(const void* x, int x_dtype, const void* res, int res_dtype, void* xsum,
+                                      const void* w, const void* b, int w_dtype, void* y, int y_dtype,
+                                      float* mean, float* rstd, int64_t rows, int64_t C, double eps,
+                                      void* stream) {
+    clear_error();
+    if (res == nullptr || xsum == nullptr)
+        return set_error(ESA_ERR_INVALID_ARGUMENT, "add layer norm: null res or xsum");
+    return layer_norm_fwd(x, x_dtype, res, res_dtype, xsum, w, b, w_dtype, y, y_dtype, mean, rstd, rows, C,
+                          eps, static_cast<cudaStream_t>(stream));
 }
 
 ESA_EXPORT size_t esa_layer_norm_workspace_bytes(int64_t rows, int64_t C) {
@@ -79,16 +90,34 @@ ESA_EXPORT size_t esa_layer_norm_workspace_bytes(int64_t rows, int64_t C) {
     return (size_t)layer_norm_partial_rows(rows > 0 ? rows : 1) * 2 * (size_t)C * sizeof(float);
 }
 
+static int ln_workspace_ok(void* workspace, size_t workspace_bytes, int64_t rows, int64_t C) {
+    const size_t need = (size_t)layer_norm_partial_rows(rows > 0 ? rows : 1) * 2 * (size_t)(C > 0 ? C : 0) *
+                        sizeof(float);
+    if (workspace == nullptr || workspace_bytes < need)
+        return set_error(ESA_ERR_WORKSPACE, "layer norm backward: workspace smaller than esa_layer_norm_workspace_bytes()");
+    return ESA_OK;
+}
+
 ESA_EXPORT int esa_layer_norm_bwd(const void* dy, int dy_dtype, const void* x, int x_dtype, const void* w,
                                   int w_dtype, const float* mean, const float* rstd, void* dx, void* dw,
                                   void* db, void* workspace, size_t workspace_bytes, int64_t rows, int64_t C,
                                   void* stream) {
     clear_error();
-    const size_t need = (size_t)layer_norm_partial_rows(rows > 0 ? rows : 1) * 2 * (size_t)(C > 0 ? C : 0) * sizeof(float);
-    if (workspace == nullptr || workspace_bytes < need)
-        return set_error(ESA_ERR_WORKSPACE, "layer norm backward: workspace smaller than esa_layer_norm_workspace_bytes()");
-    return layer_norm_bwd(dy, dy_dtype, x, x_dtype, w, w_dtype, mean, rstd, dx, dw, db,
+    if (int rc = ln_workspace_ok(workspace, workspace_bytes, rows, C)) return rc;
+    return layer_norm_bwd(dy, dy_dtype, nullptr, 0, x, x_dtype, w, w_dtype, mean, rstd, dx, nullptr, 0, dw, db,
                           static_cast<float*>(workspace), rows, C, static_cast<cudaStream_t>(stream));
+}
+
+ESA_EXPORT int esa_add_layer_norm_bwd(const void* dy, int dy_dtype, const void* dsum, int dsum_dtype,
+                                      const void* xsum, int x_dtype, const void* w, int w_dtype,
+                                      const float* mean, const float* rstd, void* dx, void* dres,
+                                      int res_dtype, void* dw, void* db, void* workspace,
+                                      size_t workspace_bytes, int64_t rows, int64_t C, void* stream) {
+    clear_error();
+    if (int rc = ln_workspace_ok(workspace, workspace_bytes, rows, C)) return rc;
+    return layer_norm_bwd(dy, dy_dtype, dsum, dsum_dtype, xsum, x_dtype, w, w_dtype, mean, rstd, dx, dres,
+                          res_dtype, dw, db, static_cast<float*>(workspace), rows, C,
+                          static_cast<cudaStream_t>(stream));
 }
 
 ESA_EXPORT int esa_wait_selftest(unsigned int* completed, unsigned int* waited_ms, void* stream) {

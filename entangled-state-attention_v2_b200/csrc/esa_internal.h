@@ -111,11 +111,12 @@ int scan_fwd_host(const void* A, const void* B, void* E, int64_t nb, int64_t T, 
                   int compass, void* staging, size_t staging_bytes, cudaStream_t s);
 int wait_selftest(unsigned* completed, unsigned* waited_ms, cudaStream_t s);
 int layer_norm_partial_rows(int64_t rows);
-int layer_norm_fwd(const void* x, int xdt, const void* w, const void* b, int wdt, void* y, int ydt,
-                   float* mean, float* rstd, int64_t rows, int64_t C, double eps, cudaStream_t s);
-int layer_norm_bwd(const void* dy, int dydt, const void* x, int xdt, const void* w, int wdt,
-                   const float* mean, const float* rstd, void* dx, void* dw, void* db, float* partial,
-                   int64_t rows, int64_t C, cudaStream_t s);
+int layer_norm_fwd(const void* x, int xdt, const void* res, int rdt, void* xsum, const void* w,
+                   const void* b, int wdt, void* y, int ydt, float* mean, float* rstd, int64_t rows, int64_t C,
+                   double eps, cudaStream_t s);
+int layer_norm_bwd(const void* dy, int dydt, const void* dsum, int dsdt, const void* x, int xdt,
+                   const void* w, int wdt, const float* mean, const float* rstd, void* dx, void* dres, int rdt,
+                   void* dw, void* db, float* partial, int64_t rows, int64_t C, cudaStream_t s);
 int readout_fwd(const void* q, int64_t qrs, int qdt, const void* E, int64_t ers, int edt, void* y,
                 int64_t yrs, int ydt, void* rstd, int64_t rows, int64_t C, double eps, cudaStream_t s);
 int readout_bwd(const void* dy, int64_t dyrs, int dydt, const void* q, int64_t qrs, int qdt, const void* E,

@@ -10,8 +10,13 @@
 // directly (the same values: one rounding of the fp32 result), and the
 // backward takes the Linear's 16-bit input gradient without the cast back.
 //
-// Forward: one warp per row of C channels (mean, then the variance about it,
-// then the outputs; arithmetic in fp32); the row's mean and rstd are kept.
+// Forward: one warp per row of C channels, the row held in registers (one
+// read; mean, then the variance about it, then the outputs; arithmetic in
+// fp32); the row's mean and rstd are kept.  Optionally fused with the
+// residual add before it: xsum = x + res is written (rounded to x's dtype, as
+// the separate add would) and normalised; the backward then adds xsum's own
+// gradient into dx and writes dx a second time in res's dtype (the gradient
+// of res).
 // Backward, per row: xhat = (x - mean) rstd, g = dy w,
 //   dx = rstd (g - mean_C(g) - xhat mean_C(g xhat));
 // the column sums dw = sum_rows dy xhat, db = sum_rows dy are accumulated per
@@ -35,6 +40,15 @@ constexpr int kLnMaxChunks = 8;  // 8-channel chunks per lane: C <= 2048
 struct LnArgs {
     const char* x;
     int xdt, xes;
+    // fused residual add (forward): xsum = x + res in x's dtype, normalised
+    const char* res;
+    int rdt, res_es;
+    char* xsum;
+    // backward: optional gradient of xsum added to dx; optional second copy
+    // of dx in res's dtype (the gradient of res)
+    const char* dsum;
+    int dsdt, dses;
+    char* dres;
     const char* w;
     const char* b;
     int wdt, wes;
@@ -50,6 +64,7 @@ struct LnArgs {
     float eps;
 };
 
+template <int NCH>
 __global__ void __launch_bounds__(32 * kLnWarps) ln_fwd_kernel(const LnArgs a) {
     const int lane = threadIdx.x & 31;
     const int64_t nw = (int64_t)gridDim.x * kLnWarps;
@@ -57,33 +72,50 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_fwd_kernel(const LnArgs a) {
     for (int64_t row = (int64_t)blockIdx.x * kLnWarps + (threadIdx.x >> 5); row < a.rows; row += nw) {
         const char* xr = a.x + row * a.C * a.xes;
         char* yr = a.y + row * a.C * a.yes;
+        // the row stays in registers: one read of x (and res), three reductions
+        float v[NCH][8];
         float s = 0.f;
-        for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
-            float v[8];
-            load8(xr + c0 * a.xes, a.xdt, v);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) s += v[i];
+        for (int k = 0; k < NCH; ++k) {
+            const int64_t c0 = lane * 8 + k * 256;
+            if (c0 < a.C) {
+                load8(xr + c0 * a.xes, a.xdt, v[k]);
+                if (a.res != nullptr) {
+                    // xsum = x + res, rounded to x's dtype as a separate add would be
+                    float u[8];
+                    load8(a.res + (row * a.C + c0) * a.res_es, a.rdt, u);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[k][i] = round_dt(v[k][i] + u[i], a.xdt);
+                    store8(a.xsum + (row * a.C + c0) * a.xes, a.xdt, v[k]);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) s += v[k][i];
+            }
         }
         const float mu = warp_sum(s) * inv_c;
         float q = 0.f;
-        for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
-            float v[8];
-            load8(xr + c0 * a.xes, a.xdt, v);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float d = v[i] - mu;
-                q = fmaf(d, d, q);
-            }
+        for (int k = 0; k < NCH; ++k) {
+            const int64_t c0 = lane * 8 + k * 256;
+            if (c0 < a.C)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float d = v[k][i] - mu;
+                    q = fmaf(d, d, q);
+                }
         }
         const float r = rsqrt_acc(warp_sum(q) * inv_c + a.eps);
-        for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
-            float v[8], w[8], bb[8], o[8];
-            load8(xr + c0 * a.xes, a.xdt, v);
-            load8(a.w + c0 * a.wes, a.wdt, w);
-            load8(a.b + c0 * a.wes, a.wdt, bb);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = fmaf((v[i] - mu) * r, w[i], bb[i]);
-            store8(yr + c0 * a.yes, a.ydt, o);
+        for (int k = 0; k < NCH; ++k) {
+            const int64_t c0 = lane * 8 + k * 256;
+            if (c0 < a.C) {
+                float w[8], bb[8], o[8];
+                load8(a.w + c0 * a.wes, a.wdt, w);
+                load8(a.b + c0 * a.wes, a.wdt, bb);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = fmaf((v[k][i] - mu) * r, w[i], bb[i]);
+                store8(yr + c0 * a.yes, a.ydt, o);
+            }
         }
         if (lane == 0) {
             a.mean[row] = mu;
@@ -143,7 +175,14 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_kernel(const LnArgs a) {
                     const float xh = (v[i] - mu) * r;
                     o[i] = r * (d[i] * w[i] - mg - xh * mgx);
                 }
+                if (a.dsum != nullptr) {
+                    float ds[8];
+                    load8(a.dsum + (row * a.C + c0) * a.dses, a.dsdt, ds);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) o[i] += ds[i];
+                }
                 store8(dxr + c0 * a.xes, a.xdt, o);
+                if (a.dres != nullptr) store8(a.dres + (row * a.C + c0) * a.res_es, a.rdt, o);
             }
         }
     }
@@ -220,8 +259,9 @@ int ln_bwd_grid(int64_t rows) {
 
 int layer_norm_partial_rows(int64_t rows) { return ln_bwd_grid(rows); }
 
-int layer_norm_fwd(const void* x, int xdt, const void* w, const void* b, int wdt, void* y, int ydt,
-                   float* mean, float* rstd, int64_t rows, int64_t C, double eps, cudaStream_t s) {
+int layer_norm_fwd(const void* x, int xdt, const void* res, int rdt, void* xsum, const void* w,
+                   const void* b, int wdt, void* y, int ydt, float* mean, float* rstd, int64_t rows, int64_t C,
+                   double eps, cudaStream_t s) {
     if (rows < 0 || C <= 0 || C % 8 != 0 || C > 256 * kLnMaxChunks)
         return set_error(ESA_ERR_INVALID_ARGUMENT, "layer norm: C must be a positive multiple of 8, at most 2048");
     if (rows == 0) return ESA_OK;
@@ -231,6 +271,14 @@ int layer_norm_fwd(const void* x, int xdt, const void* w, const void* b, int wdt
     if (int rc = ln_check(b, wdt, C, "b", &a.wes)) return rc;
     if (int rc = ln_check(y, ydt, C, "y", &a.yes)) return rc;
     if (!mean || !rstd) return set_error(ESA_ERR_INVALID_ARGUMENT, "layer norm: null mean/rstd");
+    if (res != nullptr) {
+        int es = 0;
+        if (int rc = ln_check(res, rdt, C, "res", &a.res_es)) return rc;
+        if (int rc = ln_check(xsum, xdt, C, "xsum", &es)) return rc;
+        a.res = static_cast<const char*>(res);
+        a.rdt = rdt;
+        a.xsum = static_cast<char*>(xsum);
+    }
     a.x = static_cast<const char*>(x);
     a.xdt = xdt;
     a.w = static_cast<const char*>(w);
@@ -243,15 +291,25 @@ int layer_norm_fwd(const void* x, int xdt, const void* w, const void* b, int wdt
     a.rows = rows;
     a.C = C;
     a.eps = (float)eps;
-    ln_fwd_kernel<<<ln_grid(rows), 32 * kLnWarps, 0, s>>>(a);
+    const int grid = ln_grid(rows);
+    switch ((C + 255) / 256) {
+        case 1: ln_fwd_kernel<1><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
+        case 2: ln_fwd_kernel<2><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
+        case 3: ln_fwd_kernel<3><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
+        case 4: ln_fwd_kernel<4><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
+        case 5: ln_fwd_kernel<5><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
+        case 6: ln_fwd_kernel<6><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
+        case 7: ln_fwd_kernel<7><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
+        default: ln_fwd_kernel<8><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
+    }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("layer norm launch: ") + cudaGetErrorString(e));
     return ESA_OK;
 }
 
-int layer_norm_bwd(const void* dy, int dydt, const void* x, int xdt, const void* w, int wdt,
-                   const float* mean, const float* rstd, void* dx, void* dw, void* db, float* partial,
-                   int64_t rows, int64_t C, cudaStream_t s) {
+int layer_norm_bwd(const void* dy, int dydt, const void* dsum, int dsdt, const void* x, int xdt,
+                   const void* w, int wdt, const float* mean, const float* rstd, void* dx, void* dres, int rdt,
+                   void* dw, void* db, float* partial, int64_t rows, int64_t C, cudaStream_t s) {
     if (rows < 0 || C <= 0 || C % 8 != 0 || C > 256 * kLnMaxChunks)
         return set_error(ESA_ERR_INVALID_ARGUMENT, "layer norm: C must be a positive multiple of 8, at most 2048");
     LnArgs a{};
@@ -263,6 +321,16 @@ int layer_norm_bwd(const void* dy, int dydt, const void* x, int xdt, const void*
     if (int rc = ln_check(db, wdt, C, "db", &es)) return rc;
     if (int rc = ln_check(dy, dydt, C, "dy", &a.dyes)) return rc;
     if (!mean || !rstd || !partial) return set_error(ESA_ERR_INVALID_ARGUMENT, "layer norm: null buffer");
+    if (dsum != nullptr) {
+        if (int rc = ln_check(dsum, dsdt, C, "dsum", &a.dses)) return rc;
+        a.dsum = static_cast<const char*>(dsum);
+        a.dsdt = dsdt;
+    }
+    if (dres != nullptr) {
+        if (int rc = ln_check(dres, rdt, C, "dres", &a.res_es)) return rc;
+        a.dres = static_cast<char*>(dres);
+        a.rdt = rdt;
+    }
     a.x = static_cast<const char*>(x);
     a.xdt = xdt;
     a.w = static_cast<const char*>(w);

@@ -117,6 +117,13 @@ __device__ __forceinline__ A warp_sum(A x) {
     return x;
 }
 
+// x rounded to the element type `dt` (returned widened again)
+__device__ __forceinline__ float round_dt(float x, int dt) {
+    if (dt == ESA_DTYPE_F16) return __half2float(__float2half_rn(x));
+    if (dt == ESA_DTYPE_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+    return x;
+}
+
 __device__ __forceinline__ float rsqrt_acc(float x) { return 1.0f / sqrtf(x); }
 __device__ __forceinline__ double rsqrt_acc(double x) { return 1.0 / sqrt(x); }
 

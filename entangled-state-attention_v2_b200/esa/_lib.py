@@ -42,6 +42,10 @@ SIGNATURES = {
                                _int, _vp, _i64, _int, _i64, _i64, _f64, _vp]),
     "esa_layer_norm_fwd": (_int, [_vp, _int, _vp, _vp, _int, _vp, _int, _vp, _vp, _i64, _i64, _f64, _vp]),
     "esa_layer_norm_workspace_bytes": (_sz, [_i64, _i64]),
+    "esa_add_layer_norm_fwd": (_int, [_vp, _int, _vp, _int, _vp, _vp, _vp, _int, _vp, _int, _vp, _vp, _i64,
+                                      _i64, _f64, _vp]),
+    "esa_add_layer_norm_bwd": (_int, [_vp, _int, _vp, _int, _vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _int,
+                                      _vp, _vp, _vp, _sz, _i64, _i64, _vp]),
     "esa_layer_norm_bwd": (_int, [_vp, _int, _vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64,
                                   _i64, _vp]),
     "esa_wait_selftest": (_int, [ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_uint), _vp]),

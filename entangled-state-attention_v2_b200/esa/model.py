@@ -99,6 +99,20 @@ class _LayerNorm(nn.Module):
             return y
         return F.layer_norm(x, self.weight.shape, self.weight, self.bias, 1e-5)
 
+    def add_forward(self, x: torch.Tensor, res: torch.Tensor):
+        """(x + res, LayerNorm(x + res)): the residual add and the norm after it,
+        one fused kernel on the GPU (the sum in x's dtype, as `x + res`)."""
+        if (ops.layer_norm_supported(x, self.weight, self.bias) and res.is_cuda
+                and res.shape == x.shape and torch.result_type(x, res) == x.dtype
+                and res.dtype in (torch.float16, torch.bfloat16, torch.float32)):
+            out_dtype = x.dtype
+            if torch.is_autocast_enabled("cuda"):
+                out_dtype = torch.get_autocast_dtype("cuda")
+            xsum, y, _, _ = ops.add_layer_norm(x, res, self.weight, self.bias, 1e-5, out_dtype)
+            return xsum, y
+        x = x + res
+        return x, self(x)
+
 
 class _MLP(nn.Module):
     def __init__(self, cfg: ESAModelConfig):
@@ -122,8 +136,19 @@ class _ESABlock(nn.Module):
         self.mlp = _MLP(cfg)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        x = x + self.esa(self.ln1(x))
-        return x + self.mlp(self.ln2(x))
+        x, h = self.ln2.add_forward(x, self.esa(self.ln1(x)))
+        return x + self.mlp(h)
+
+    def fused_forward(self, x: torch.Tensor, pending: torch.Tensor | None):
+        """forward(x + pending) returned as (x', pending'): the block's residual
+        adds fused into the norms after them.  `pending` is the previous
+        block's MLP output not yet added to x; the caller adds the last one."""
+        if pending is None:
+            h = self.ln1(x)
+        else:
+            x, h = self.ln1.add_forward(x, pending)
+        x, h = self.ln2.add_forward(x, self.esa(h))
+        return x, self.mlp(h)
 
     @torch.no_grad()
     def prefill(self, x: torch.Tensor, *, backend: str | None = None, compass: int | None = None):
@@ -135,8 +160,19 @@ class _ESABlock(nn.Module):
 
     def lightning_step(self, x: torch.Tensor, state: torch.Tensor):
         y, new_state = self.esa.decode_step(self.ln1(x), state)
-        x = x + y
-        return x + self.mlp(self.ln2(x)), new_state
+        x, h = self.ln2.add_forward(x, y)
+        return x + self.mlp(h), new_state
+
+    def fused_lightning_step(self, x: torch.Tensor, pending: torch.Tensor | None, state: torch.Tensor):
+        """lightning_step(x + pending) as (x', pending', new state), the residual
+        adds fused into the norms (see fused_forward)."""
+        if pending is None:
+            h = self.ln1(x)
+        else:
+            x, h = self.ln1.add_forward(x, pending)
+        y, new_state = self.esa.decode_step(h, state)
+        x, h = self.ln2.add_forward(x, y)
+        return x, self.mlp(h), new_state
 
 
 def _resolve_device(device) -> torch.device:
@@ -229,9 +265,11 @@ class ESAModel(nn.Module):
             raise ValueError(f"Sequence length {T} exceeds block {self.config.block}.")
         pos = torch.arange(T, dtype=torch.long, device=input_ids.device)
         x = self.drop(self.wte(input_ids) + self.wpe(pos)[None, :, :])
+        pending = None
         for block in self.blocks:
-            x = block(x)
-        logits = self.lm_head(self.ln_f(x))
+            x, pending = block.fused_forward(x, pending)
+        h = self.ln_f(x) if pending is None else self.ln_f.add_forward(x, pending)[1]
+        logits = self.lm_head(h)
         loss = None
         if targets is not None:
             loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1),
@@ -343,10 +381,12 @@ class ESAModel(nn.Module):
         """One recurrent decode step over all layers; returns (logits, new states)."""
         x = self.drop(self.wte(token) + self.wpe(pos_tensor)[None, :])
         new_states = []
+        pending = None
         for index, block in enumerate(self.blocks):
-            x, s = block.lightning_step(x, states[index])
+            x, pending, s = block.fused_lightning_step(x, pending, states[index])
             new_states.append(s)
-        return self.lm_head(self.ln_f(x)), torch.stack(new_states, dim=0).contiguous()
+        h = self.ln_f(x) if pending is None else self.ln_f.add_forward(x, pending)[1]
+        return self.lm_head(h), torch.stack(new_states, dim=0).contiguous()
 
     def compile_generation(self, *, mode: str = "default", fullgraph: bool = False) -> "ESAModel":
         """torch.compile the fixed-shape decode step (the reference's runtime)."""

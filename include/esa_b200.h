@@ -99,6 +99,24 @@ int esa_layer_norm_bwd(const void *dy, int dy_dtype, const void *x, int x_dtype,
                        int w_dtype, const float *mean, const float *rstd, void *dx, void *dw, void *db,
                        void *workspace, size_t workspace_bytes, int64_t rows, int64_t C, void *stream);
 
+/* esa_layer_norm_fwd fused with the residual add before it:
+ *   xsum = x + res   (written in x's dtype, rounded as a separate add is)
+ *   y    = LayerNorm(xsum)
+ * res has its own dtype (e.g. the fp16 output of a Linear under autocast added
+ * to an fp32 residual stream).  Replaces `x = x + branch(...)` followed by
+ * `ln(x)` in the ESAModel blocks (esa/model.py of the reference). */
+int esa_add_layer_norm_fwd(const void *x, int x_dtype, const void *res, int res_dtype, void *xsum,
+                           const void *w, const void *b, int w_dtype, void *y, int y_dtype, float *mean,
+                           float *rstd, int64_t rows, int64_t C, double eps, void *stream);
+
+/* Gradient of esa_add_layer_norm_fwd: dx = LayerNorm backward at xsum (+ dsum,
+ * the gradient of xsum, when not NULL) in x's dtype; dres (nullable) the same
+ * values in res's dtype; dw, db as esa_layer_norm_bwd. */
+int esa_add_layer_norm_bwd(const void *dy, int dy_dtype, const void *dsum, int dsum_dtype,
+                           const void *xsum, int x_dtype, const void *w, int w_dtype, const float *mean,
+                           const float *rstd, void *dx, void *dres, int res_dtype, void *dw, void *db,
+                           void *workspace, size_t workspace_bytes, int64_t rows, int64_t C, void *stream);
+
 /* Diagnostic: runs the kernels' bounded mbarrier wait on a barrier that never
  * completes, on `stream`, and synchronises it.  The wait gives up after its
  * one-second budget: *completed = 0, *waited_ms = the time waited, and
