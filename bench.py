@@ -47,6 +47,12 @@ def _peaks():
     return 6650.0, "fallback"
 
 
+KERNEL_NAMES = {
+    "lane": "lane_scan_kernel<FwdPlain, __half, __half, NW> (one lane per channel pair, steps in order)",
+    "strip": "strip_scan_kernel<FwdPlain, __half, __half, LPR, SR> (strip width chosen per shape)",
+}
+
+
 def _traffic_summary():
     p = ROOT / "profiles" / "roofline_traffic.json"
     if p.exists():
@@ -236,6 +242,7 @@ def run_ours(args) -> None:
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize(dev)
+    path = _lib.last_scan_path()  # kernel family the timed launches use
 
     clocks = ClockSampler(local)
     clocks.start()
@@ -333,7 +340,7 @@ def run_ours(args) -> None:
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "mean_launch_ms": mean_launch_ms,
-                         "kernel": "strip_scan_kernel<FwdPlain, __half, __half, LPR, SR> (strip width chosen per shape)",
+                         "kernel": KERNEL_NAMES.get(path, path),
                          "traffic": (traffic or {}).get("bytes_per_launch"),
                          "traffic_source": (traffic or {}).get("source")},
             "cpu_baseline": None,

@@ -19,6 +19,10 @@ int set_error(int code, const std::string& msg) {
 
 void clear_error() { t_last_error.clear(); }
 
+static thread_local int t_last_path = 0;
+void note_scan_path(int path) { t_last_path = path; }
+int last_scan_path() { return t_last_path; }
+
 int device_sm_count(int device) {
     static int cache[64] = {0};
     static std::mutex mu;
@@ -45,6 +49,8 @@ extern "C" {
 ESA_EXPORT int esa_abi_version(void) { return ESA_ABI_VERSION; }
 
 ESA_EXPORT const char* esa_last_error(void) { return t_last_error.c_str(); }
+
+ESA_EXPORT int esa_scan_last_path(void) { return last_scan_path(); }
 
 ESA_EXPORT int esa_readout_fwd(const void* q, int64_t q_row_stride, int q_dtype, const void* E,
                                int64_t e_row_stride, int e_dtype, void* y, int64_t y_row_stride,

@@ -14,6 +14,9 @@ namespace esa {
 int set_error(int code, const std::string& msg);
 // Clears this thread's last error.
 void clear_error();
+// Kernel family of the last scan launch on this host thread (ESA_PATH_*).
+void note_scan_path(int path);
+int last_scan_path();
 // Number of SMs of `device` (cached).
 int device_sm_count(int device);
 // Device address of the status word on `device` (cached; null on failure).

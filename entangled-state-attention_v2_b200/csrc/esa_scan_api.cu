@@ -29,7 +29,60 @@ int strip_rev_gated(const ScanCall& c, bool* taken);
 int strip_fwd_summary(const ScanCall& c, bool* taken);
 int strip_summary_launch(const ScanCall& c, bool* taken);
 
+int lane_fwd_plain(const ScanCall& c, bool* taken, double min_warps);
+int lane_fwd_summary(const ScanCall& c, bool* taken, double min_warps);
+int lane_rev_plain(const ScanCall& c, bool* taken, double min_warps);
+int lane_fwd_gated(const ScanCall& c, bool* taken, double min_warps);
+int lane_rev_gated(const ScanCall& c, bool* taken, double min_warps);
+
+namespace {
+// ESA_SCAN_PATH: "lane" (lane-serial whenever it applies), "strip" (never
+// lane-serial), "lookback" (see run()); unset: automatic.
+std::string scan_path_env() {
+    const char* v = getenv("ESA_SCAN_PATH");
+    return v != nullptr ? std::string(v) : std::string();
+}
+}  // namespace
+
+// Lane-serial scan (esa_lane.cuh) when the channels give every SM at least
+// kLaneMinWarps consumer warps.  Automatic only for the plain forward scan of
+// 16-bit data and its summary pass; every other kind keeps the strip scan
+// unless ESA_SCAN_PATH=lane (the lane form's reverse and gated steps ran
+// slower on B200: one lane per channel vector cannot hide their longer
+// per-step latency).
+constexpr double kLaneMinWarps = 2.0;
+
+int lane_scan_launch(const ScanCall& c, bool* taken) {
+    static const std::string path = scan_path_env();
+    *taken = false;
+    if (path == "strip") return ESA_OK;
+    const bool forced = path == "lane";
+    const double mw = forced ? 0.0 : kLaneMinWarps;
+    const bool fwd16 = (c.kind == Kind::FwdPlain || c.kind == Kind::FwdSummary) && dtype_size(c.te) == 2;
+    if (!forced && !fwd16) return ESA_OK;
+    if (c.summ || c.kind == Kind::FwdSummary) {
+        switch (c.kind) {
+            case Kind::FwdPlain:
+            case Kind::FwdSummary: return lane_fwd_summary(c, taken, mw);
+            case Kind::RevPlain: return lane_rev_plain(c, taken, mw);
+            case Kind::FwdGated: return lane_fwd_gated(c, taken, mw);
+            case Kind::RevGated: return lane_rev_gated(c, taken, mw);
+        }
+        return ESA_OK;
+    }
+    switch (c.kind) {
+        case Kind::FwdPlain: return lane_fwd_plain(c, taken, mw);
+        case Kind::RevPlain: return lane_rev_plain(c, taken, mw);
+        case Kind::FwdGated: return lane_fwd_gated(c, taken, mw);
+        case Kind::RevGated: return lane_rev_gated(c, taken, mw);
+        case Kind::FwdSummary: return lane_fwd_summary(c, taken, mw);
+    }
+    return ESA_OK;
+}
+
 int strip_scan_launch(const ScanCall& c, bool* taken) {
+    if (int rc = lane_scan_launch(c, taken)) return rc;
+    if (*taken) return ESA_OK;
     if (c.summ) return strip_summary_launch(c, taken);
     switch (c.kind) {
         case Kind::FwdPlain: return strip_fwd_plain(c, taken);
@@ -59,7 +112,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 bool encode_strip_map(CUtensorMap* map, int dtype, const void* base, int64_t nb, int64_t T,
-                      int64_t hd, int64_t rs, int ws, int lt, std::string* err) {
+                      int64_t hd, int64_t rs, int ws, int lt, std::string* err, int promo_bytes) {
     auto fn = encode_fn();
     if (!fn) {
         *err = "cuTensorMapEncodeTiled unavailable";
@@ -80,7 +133,11 @@ bool encode_strip_map(CUtensorMap* map, int dtype, const void* base, int64_t nb,
     const cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    promo_bytes >= 256   ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+                    : promo_bytes >= 128 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B
+                    : promo_bytes >= 64  ? CU_TENSOR_MAP_L2_PROMOTION_L2_64B
+                                         : CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         *err = "cuTensorMapEncodeTiled error " + std::to_string((int)r);
         return false;
@@ -173,6 +230,7 @@ int seq_typed(const ScanCall& c) {
     const int threads = 256;
     const int64_t nch = c.a.nb * c.a.hd;
     const int64_t blocks = (nch + threads - 1) / threads;
+    note_scan_path(ESA_PATH_SEQUENTIAL);
     sequential_scan_kernel<K, Tin, Te><<<(unsigned)blocks, threads, 0, c.stream>>>(c.a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("sequential scan launch: ") + cudaGetErrorString(e));

@@ -522,6 +522,7 @@ int launch_typed(const ScanCall& call) {
     if (e != cudaSuccess || per_sm <= 0) return set_error(ESA_ERR_CUDA, "lookback scan kernel cannot be resident");
     int64_t grid = (int64_t)per_sm * device_sm_count(dev);
     if (grid > geo.ntiles) grid = geo.ntiles;
+    note_scan_path(ESA_PATH_LOOKBACK);
     lookback_scan_kernel<K, Tin, Te><<<(unsigned)grid, 32 * geo.nwarp, smem, call.stream>>>(prm);
     e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("lookback scan launch: ") + cudaGetErrorString(e));

@@ -460,9 +460,10 @@ inline int strip_env(const char* name) {
 }
 
 // Build a 3-D tensor map [nb][T][hd] (row stride rs elements) with box
-// [1][LT][WS] for dtype code `dtype`.
+// [1][LT][WS] for dtype code `dtype`; L2 promotion of `promo_bytes` (256,
+// 128, 64 or 0 = none).
 bool encode_strip_map(CUtensorMap* map, int dtype, const void* base, int64_t nb, int64_t T,
-                      int64_t hd, int64_t rs, int ws, int lt, std::string* err);
+                      int64_t hd, int64_t rs, int ws, int lt, std::string* err, int promo_bytes = 256);
 
 template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM>
 int strip_launch_typed(const ScanCall& call, int nstage, int grid) {
@@ -496,6 +497,7 @@ int strip_launch_typed(const ScanCall& call, int nstage, int grid) {
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("strip smem attribute: ") + cudaGetErrorString(e));
     if (grid > prm.nitems) grid = (int)prm.nitems;
+    note_scan_path(ESA_PATH_STRIP);
     strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM><<<grid, Cfg::NT, smem, call.stream>>>(prm, maps[0], maps[1],
                                                                                   maps[2], maps[3]);
     e = cudaGetLastError();
@@ -564,9 +566,15 @@ int strip_launch_kind(const ScanCall& call, bool* taken) {
         if (n < (sms * 3) / 4) continue;  // too few strips to fill the GPU
         // two stages (measured: never slower than 3-6, and 8 % faster on the
         // [32,4096,16,64] fp16 forward -- 5.84 vs 5.38 TB/s -- with the same
-        // occupancy); more only if two do not fit
+        // occupancy); more only if two do not fit.  The 16-bit reverse takes
+        // three when they keep the occupancy of two (237.8 vs 243.9 us on
+        // [32,4096,16,64] fp16: its stages hold 32 steps, not 64).
         int ns = 0, o = 0;
-        for (int s = 2; s <= 6; ++s) {
+        if (!force_ns && K == Kind::RevPlain && sizeof(Te) == 2 && occ(lpr, 3) >= occ(lpr, 2) && occ(lpr, 3) > 0) {
+            ns = 3;
+            o = occ(lpr, 3);
+        }
+        for (int s = 2; s <= 6 && ns == 0; ++s) {
             if (force_ns && s != force_ns) continue;
             const int os = occ(lpr, s);
             if (os > o) {

@@ -35,6 +35,7 @@ _sz = ctypes.c_size_t
 SIGNATURES = {
     "esa_abi_version": (_int, []),
     "esa_last_error": (ctypes.c_char_p, []),
+    "esa_scan_last_path": (_int, []),
     "esa_device_status": (_int, [_int, _int, ctypes.POINTER(ctypes.c_uint)]),
     "esa_readout_fwd": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _i64,
                                _f64, _vp]),
@@ -111,6 +112,15 @@ def check(rc: int, what: str) -> None:
     if rc == -2:
         raise TypeError(f"{what}: {msg}")
     raise RuntimeError(f"{what} failed ({rc}): {msg}")
+
+
+SCAN_PATHS = {0: "none", 1: "sequential", 2: "lookback", 3: "strip", 4: "lane"}
+
+
+def last_scan_path() -> str:
+    """Kernel family of the last scan launch on this host thread: "sequential",
+    "lookback", "strip" or "lane" ("none" before any)."""
+    return SCAN_PATHS.get(int(lib().esa_scan_last_path()), "unknown")
 
 
 def device_status(device: int, clear: bool = True) -> int:

@@ -125,6 +125,20 @@ int esa_add_layer_norm_bwd(const void *dy, int dy_dtype, const void *dsum, int d
  * a hang.  No reference counterpart. */
 int esa_wait_selftest(unsigned int *completed, unsigned int *waited_ms, void *stream);
 
+/* Kernel family of the last scan launch on this host thread (diagnostics and
+ * tests): ESA_PATH_NONE before any, ESA_PATH_SEQUENTIAL (one thread per
+ * channel, any alignment), ESA_PATH_LOOKBACK (time chunks, decoupled
+ * look-back), ESA_PATH_STRIP (channel strips, tile-parallel steps),
+ * ESA_PATH_LANE (channel strips, one lane per channel vector walking the
+ * steps in order).  A split scan reports its output pass.  No reference
+ * counterpart. */
+#define ESA_PATH_NONE 0
+#define ESA_PATH_SEQUENTIAL 1
+#define ESA_PATH_LOOKBACK 2
+#define ESA_PATH_STRIP 3
+#define ESA_PATH_LANE 4
+int esa_scan_last_path(void);
+
 /* Version of this ABI (ESA_ABI_VERSION). */
 int esa_abi_version(void);
 

@@ -21,7 +21,7 @@ def _declared_symbols():
 def test_header_declares_the_abi():
     syms = _declared_symbols()
     assert set(syms) == {
-        "esa_abi_version", "esa_last_error", "esa_device_status", "esa_scan_workspace_bytes",
+        "esa_abi_version", "esa_last_error", "esa_scan_last_path", "esa_device_status", "esa_scan_workspace_bytes",
         "esa_scan_fwd", "esa_scan_rev", "esa_gated_scan_fwd", "esa_gated_scan_bwd",
         "esa_lightning_step", "esa_scan_fwd_noalloc", "esa_scan_summary",
         "esa_scan_host_staging_bytes", "esa_scan_fwd_host", "esa_scan_fwd_resume",
