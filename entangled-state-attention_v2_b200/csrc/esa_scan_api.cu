@@ -3,7 +3,10 @@
 //
 // Path choice for every scan kind:
 //   1. strip scan (esa_strip.cuh) when every row is 16-byte aligned and there
-//      are enough channels to fill the GPU with channel strips;
+//      are enough channels to fill the GPU with channel strips -- for the
+//      plain forward of 16-bit data (and its summary pass) with at least two
+//      warps' worth of channel pairs per SM, its lane-serial form
+//      (esa_lane.cuh: one lane per channel pair walking the steps in order);
 //   2. few channels and a long time axis: the split scan -- every batch row
 //      cut into time pieces that the strip scan treats as rows: a summary
 //      pass (each piece's end state from zero and its coefficient product),
