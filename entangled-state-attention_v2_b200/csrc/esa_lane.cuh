@@ -192,6 +192,7 @@ __global__ void __launch_bounds__(32 * (NW + 1)) lane_scan_kernel(const StripPar
                 os0 = ka.out[0].rs * (int64_t)P::OES;
                 os1 = ka.out[1].rs * (int64_t)P::OES;
             }
+            // full tiles that do not hold step 0 run without per-step branches
             auto steps = [&](auto full_tag) {
                 constexpr bool FULLT = decltype(full_tag)::value;
 #pragma unroll
@@ -210,13 +211,13 @@ __global__ void __launch_bounds__(32 * (NW + 1)) lane_scan_kernel(const StripPar
                             vfma(e, a, e, bb);
                             vmul(prod, prod, a);
                         } else {
-                            step_apply<K, Tin, Te, 1, P>(rows, ka, g.b, t0 + r, gc, valid, e, cache, 0,
-                                                         ob0 + r * os0, ob1 + r * os1);
+                            step_apply<K, Tin, Te, 1, P, !FULLT>(rows, ka, g.b, t0 + r, gc, valid, e, cache, 0,
+                                                                 ob0 + r * os0, ob1 + r * os1);
                         }
                     }
                 }
             };
-            if (nrows == LT)
+            if (nrows == LT && t0 > 0)
                 steps(std::true_type{});
             else
                 steps(std::false_type{});

@@ -265,7 +265,9 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
 // Phase-3 step: advance the state `e` over step t and write this step's
 // outputs for VEC channels starting at global channel `gc` (when `valid`).
 // Forward: e = E_{t-1} in, E_t out.  Reverse: e = H_{t+1} in, H_t out.
-template <Kind K, typename Tin, typename Te, int S, typename P = Policy<K, Tin, Te>>
+// MAY_T0 = false promises t > 0 (the reverse kinds then read E_{t-1} from
+// shared memory with no branch on t).
+template <Kind K, typename Tin, typename Te, int S, typename P = Policy<K, Tin, Te>, bool MAY_T0 = true>
 __device__ __forceinline__ void step_apply(const char* const (&rows)[4], const KArgs& prm,
                                            int64_t b, int64_t t, int64_t gc, bool valid,
                                            typename P::acc (&e)[P::VEC],
@@ -285,7 +287,7 @@ __device__ __forceinline__ void step_apply(const char* const (&rows)[4], const K
         acc ep[VEC], d[VEC];
 #pragma unroll
         for (int i = 0; i < VEC; ++i) d[i] = cache.c1[s][i];
-        if (t > 0) {
+        if (!MAY_T0 || t > 0) {
             load_smem<Te, VEC>(K == Kind::RevPlain ? rows[1] : rows[2], ep);
         } else {
 #pragma unroll
