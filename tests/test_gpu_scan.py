@@ -150,6 +150,34 @@ def test_gated_scan_fwd_bwd_strided(raw_dtype, scan_dtype):
     assert rel(dv, dv_ref) < tol * 2
 
 
+def test_gated_scan_training_layer_shape():
+    """The ESAModel training layer [16, 2048, 768] fp16 (12 heads of 64, qgv
+    row stride 3C): forward and backward on the GPU, checked against the
+    oracle on three batch rows (the kernels run all 16)."""
+    from esa import ops
+    g = torch.Generator().manual_seed(9)
+    Bsz, T, C = 16, 2048, 768
+    qgv = torch.randn(Bsz, T, 3 * C, generator=g).half()
+    qd = qgv.to(DEV)
+    grd, vrd = qd[..., C:2 * C], qd[..., 2 * C:]
+    E, e_last = ops.gated_scan(grd, vrd, None, 0.8, 0.995, 16, torch.float16)
+    dE = torch.randn(Bsz, T, C, generator=g).half()
+    dg, dv, _ = ops.gated_scan_backward(grd, vrd, E, dE.to(DEV), None, 0.8, 0.995, 16)
+    rows = [0, 7, 15]
+    gr, vr = qgv[rows, :, C:2 * C], qgv[rows, :, 2 * C:]
+    A64, B64 = oracle.gate(gr, vr)
+    Ar = torch.from_numpy(A64).half().double().reshape(3, T, 1, C)
+    Br = torch.from_numpy(B64).half().double().reshape(3, T, 1, C)
+    ref = oracle.scan_fwd(Ar, Br).reshape(3, T, C)
+    assert rel(E[rows], ref) < 2e-3
+    assert rel(e_last[rows], ref[:, -1]) < 2e-3
+    dA, dB, _ = oracle.scan_rev(Ar, E[rows].double().cpu().reshape(3, T, 1, C),
+                                dE[rows].double().reshape(3, T, 1, C))
+    dg_ref, dv_ref = oracle.gate_bwd(gr, vr, dA.reshape(3, T, C), dB.reshape(3, T, C))
+    assert rel(dg[rows], dg_ref) < 4e-3
+    assert rel(dv[rows], dv_ref) < 4e-3
+
+
 def test_gated_autograd_through_layer_slices():
     """torch autograd through the gated op equals autograd through the
     materialised gate + thunder_scan (both on the GPU, fp64)."""
