@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "../../include/esa_b200.h"
 
 namespace esa {
@@ -170,5 +172,33 @@ __device__ __forceinline__ double sigmoid_(double x) { return 1.0 / (1.0 + exp(-
 __device__ __forceinline__ float sigmoid_(float x) { return sigmoidf_(x); }
 __device__ __forceinline__ float tanh_(float x) { return tanhf(x); }
 __device__ __forceinline__ double tanh_(double x) { return tanh(x); }
+
+// Gate nonlinearity of 16-bit logits feeding a 16-bit scan: CUDA's fast
+// intrinsics __expf and __fdividef for the sigmoid and the hardware tanh
+// approximation (PTX tanh.approx.f32, relative error below 2^-10.98).  Their
+// errors sit at the half-precision rounding (2^-11 relative) that the logits
+// carry in and that A, B and E get on the way out; the exact forms above cost
+// the fused gated scans a third of their speed (the [16,2048,768] fp16
+// forward: 115.7 vs 75.4 us).  Wider logits or scans keep the exact forms.
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float tanh_fast(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+template <bool FAST, typename A>
+__device__ __forceinline__ A gate_sigmoid(A x) {
+    if constexpr (FAST && std::is_same<A, float>::value)
+        return sigmoid_fast(x);
+    else
+        return sigmoid_(x);
+}
+template <bool FAST, typename A>
+__device__ __forceinline__ A gate_tanh(A x) {
+    if constexpr (FAST && std::is_same<A, float>::value)
+        return tanh_fast(x);
+    else
+        return tanh_(x);
+}
 
 }  // namespace esa

@@ -208,6 +208,7 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
                                           typename P::template Cache<S>& cache, int s) {
     using acc = typename P::acc;
     constexpr int VEC = P::VEC;
+    constexpr bool FASTG = sizeof(Tin) == 2 && sizeof(Te) == 2;  // 16-bit gates (gate_sigmoid)
     if constexpr (K == Kind::FwdPlain || K == Kind::FwdSummary) {
         load_smem<Tin, VEC>(rows[0], a);
         load_smem<Tin, VEC>(rows[1], b);
@@ -223,8 +224,8 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
         const acc lo = acc(prm.gmin), span = acc(prm.span);
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-            acc A = lo + span * sigmoid_(g[i]);
-            acc B = (acc(1) - A) * tanh_(v[i]);
+            acc A = lo + span * gate_sigmoid<FASTG>(g[i]);
+            acc B = (acc(1) - A) * gate_tanh<FASTG>(v[i]);
             if (prm.round_ab) {
                 A = round_to<Te>(A);
                 B = round_to<Te>(B);
@@ -251,7 +252,7 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
         const acc lo = acc(prm.gmin), span = acc(prm.span);
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-            const acc sg = sigmoid_(g[i]);
+            const acc sg = gate_sigmoid<FASTG>(g[i]);
             acc A = lo + span * sg;
             if (prm.round_ab) A = round_to<Te>(A);
             cache.c0[s][i] = sg;
@@ -275,6 +276,7 @@ __device__ __forceinline__ void step_apply(const char* const (&rows)[4], const K
                                            char* o1) {
     using acc = typename P::acc;
     constexpr int VEC = P::VEC;
+    constexpr bool FASTG = sizeof(Tin) == 2 && sizeof(Te) == 2;  // 16-bit gates (gate_sigmoid)
     if constexpr (K == Kind::FwdPlain) {
         vfma(e, cache.c0[s], e, cache.c1[s]);
         if (valid)
@@ -316,7 +318,7 @@ __device__ __forceinline__ void step_apply(const char* const (&rows)[4], const K
                 const acc sg = cache.c0[s][i];
                 const acc A = lo + span * sg;
                 const acc Ar = prm.round_ab ? round_to<Te>(A) : A;
-                const acc V = tanh_(v[i]);
+                const acc V = gate_tanh<FASTG>(v[i]);
                 const acc g = d[i] + e[i];
                 const acc dA = g * ep[i];
                 dg[i] = (dA - g * V) * span * sg * (acc(1) - sg);
