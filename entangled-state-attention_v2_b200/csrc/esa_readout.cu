@@ -16,6 +16,7 @@
 // and of its gradient, row stride 3C); every operand has its own element type.
 // Roofline: HBM -- forward reads q and E and writes y (plus 4 bytes a row);
 // backward reads dy, q, E and writes dq and dE.
+#include <initializer_list>
 #include <string>
 
 #include "../../include/esa_b200.h"
@@ -49,73 +50,90 @@ struct ReadoutArgs {
 
 constexpr int kReadoutWarps = 8;
 
-template <typename A, bool VECT>
+// FIX >= 0: every operand of the call has the 16-bit dtype code FIX (the
+// autocast training layer), so loads and stores resolve at compile time and
+// the sigmoid takes its fast 16-bit form (gate_sigmoid); FIX < 0: per-operand
+// dtypes read at run time, exact sigmoid.
+template <int FIX>
+__device__ __forceinline__ int dt_of(int dt) { return FIX >= 0 ? FIX : dt; }
+template <int FIX>
+__device__ __forceinline__ int es_of(int es) { return FIX >= 0 ? 2 : es; }
+
+template <typename A, bool VECT, int FIX>
 __global__ void __launch_bounds__(32 * kReadoutWarps) readout_fwd_kernel(const ReadoutArgs a) {
+    constexpr bool FAST = FIX >= 0;
     const int lane = threadIdx.x & 31;
     const int64_t nw = (int64_t)gridDim.x * kReadoutWarps;
     const A inv_c = A(1) / A(a.C), eps = A(a.eps);
+    const int edt = dt_of<FIX>(a.E.dt), qdt = dt_of<FIX>(a.q.dt), ydt = dt_of<FIX>(a.y.dt);
+    const int ees = es_of<FIX>(a.E.es), qes = es_of<FIX>(a.q.es), yes = es_of<FIX>(a.y.es);
     for (int64_t row = (int64_t)blockIdx.x * kReadoutWarps + (threadIdx.x >> 5); row < a.rows; row += nw) {
-        const char* er = a.E.p + row * a.E.rs * a.E.es;
-        const char* qr = a.q.p + row * a.q.rs * a.q.es;
-        char* yr = a.y.p + row * a.y.rs * a.y.es;
+        const char* er = a.E.p + row * a.E.rs * ees;
+        const char* qr = a.q.p + row * a.q.rs * qes;
+        char* yr = a.y.p + row * a.y.rs * yes;
         A ss = A(0);
         for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
             A e[8];
-            row_load<A, VECT>(er, a.E.dt, a.E.es, c0, a.C, e);
+            row_load<A, VECT>(er, edt, ees, c0, a.C, e);
 #pragma unroll
             for (int i = 0; i < 8; ++i) ss = fma_rn(e[i], e[i], ss);
         }
         const A r = rsqrt_acc(warp_sum(ss) * inv_c + eps);
         for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
             A e[8], q[8], y[8];
-            row_load<A, VECT>(er, a.E.dt, a.E.es, c0, a.C, e);
-            row_load<A, VECT>(qr, a.q.dt, a.q.es, c0, a.C, q);
+            row_load<A, VECT>(er, edt, ees, c0, a.C, e);
+            row_load<A, VECT>(qr, qdt, qes, c0, a.C, q);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) y[i] = sigmoid_(q[i]) * (e[i] * r);
-            row_store<A, VECT>(yr, a.y.dt, a.y.es, c0, a.C, y);
+            for (int i = 0; i < 8; ++i) y[i] = gate_sigmoid<FAST>(q[i]) * (e[i] * r);
+            row_store<A, VECT>(yr, ydt, yes, c0, a.C, y);
         }
         if (lane == 0) static_cast<A*>(a.rstd)[row] = r;
     }
 }
 
-template <typename A, bool VECT>
+template <typename A, bool VECT, int FIX>
 __global__ void __launch_bounds__(32 * kReadoutWarps) readout_bwd_kernel(const ReadoutArgs a) {
+    constexpr bool FAST = FIX >= 0;
     const int lane = threadIdx.x & 31;
     const int64_t nw = (int64_t)gridDim.x * kReadoutWarps;
     const A inv_c = A(1) / A(a.C);
+    const int edt = dt_of<FIX>(a.E.dt), qdt = dt_of<FIX>(a.q.dt), dydt = dt_of<FIX>(a.dy.dt);
+    const int dqdt = dt_of<FIX>(a.dq.dt), dedt = dt_of<FIX>(a.dE.dt);
+    const int ees = es_of<FIX>(a.E.es), qes = es_of<FIX>(a.q.es), dyes = es_of<FIX>(a.dy.es);
+    const int dqes = es_of<FIX>(a.dq.es), dees = es_of<FIX>(a.dE.es);
     for (int64_t row = (int64_t)blockIdx.x * kReadoutWarps + (threadIdx.x >> 5); row < a.rows; row += nw) {
-        const char* er = a.E.p + row * a.E.rs * a.E.es;
-        const char* qr = a.q.p + row * a.q.rs * a.q.es;
-        const char* dyr = a.dy.p + row * a.dy.rs * a.dy.es;
-        char* dqr = a.dq.p + row * a.dq.rs * a.dq.es;
-        char* der = a.dE.p + row * a.dE.rs * a.dE.es;
+        const char* er = a.E.p + row * a.E.rs * ees;
+        const char* qr = a.q.p + row * a.q.rs * qes;
+        const char* dyr = a.dy.p + row * a.dy.rs * dyes;
+        char* dqr = a.dq.p + row * a.dq.rs * dqes;
+        char* der = a.dE.p + row * a.dE.rs * dees;
         const A r = static_cast<const A*>(a.rstd)[row];
         // sum over the row of dn * n, dn = dy * s
         A dot = A(0);
         for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
             A e[8], q[8], dy[8];
-            row_load<A, VECT>(er, a.E.dt, a.E.es, c0, a.C, e);
-            row_load<A, VECT>(qr, a.q.dt, a.q.es, c0, a.C, q);
-            row_load<A, VECT>(dyr, a.dy.dt, a.dy.es, c0, a.C, dy);
+            row_load<A, VECT>(er, edt, ees, c0, a.C, e);
+            row_load<A, VECT>(qr, qdt, qes, c0, a.C, q);
+            row_load<A, VECT>(dyr, dydt, dyes, c0, a.C, dy);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) dot = fma_rn(dy[i] * sigmoid_(q[i]), e[i] * r, dot);
+            for (int i = 0; i < 8; ++i) dot = fma_rn(dy[i] * gate_sigmoid<FAST>(q[i]), e[i] * r, dot);
         }
         const A mdot = warp_sum(dot) * inv_c;
         for (int64_t c0 = lane * 8; c0 < a.C; c0 += 256) {
             A e[8], q[8], dy[8], dq[8], de[8];
-            row_load<A, VECT>(er, a.E.dt, a.E.es, c0, a.C, e);
-            row_load<A, VECT>(qr, a.q.dt, a.q.es, c0, a.C, q);
-            row_load<A, VECT>(dyr, a.dy.dt, a.dy.es, c0, a.C, dy);
+            row_load<A, VECT>(er, edt, ees, c0, a.C, e);
+            row_load<A, VECT>(qr, qdt, qes, c0, a.C, q);
+            row_load<A, VECT>(dyr, dydt, dyes, c0, a.C, dy);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const A s = sigmoid_(q[i]);
+                const A s = gate_sigmoid<FAST>(q[i]);
                 const A n = e[i] * r;
                 const A dn = dy[i] * s;
                 dq[i] = dy[i] * n * s * (A(1) - s);
                 de[i] = r * (dn - n * mdot);
             }
-            row_store<A, VECT>(dqr, a.dq.dt, a.dq.es, c0, a.C, dq);
-            row_store<A, VECT>(der, a.dE.dt, a.dE.es, c0, a.C, de);
+            row_store<A, VECT>(dqr, dqdt, dqes, c0, a.C, dq);
+            row_store<A, VECT>(der, dedt, dees, c0, a.C, de);
         }
     }
 }
@@ -124,31 +142,46 @@ bool vec_ok(const void* p, int64_t rs, int es) {
     return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && (rs * es) % 16 == 0;
 }
 
-template <template <typename, bool> class Launch>
-int readout_launch(const ReadoutArgs& a, bool wide, bool vect, cudaStream_t s) {
+// `fix`: the common 16-bit dtype code of every operand, or -1.
+template <template <typename, bool, int> class Launch>
+int readout_launch(const ReadoutArgs& a, bool wide, bool vect, int fix, cudaStream_t s) {
     const int64_t blocks_needed = (a.rows + kReadoutWarps - 1) / kReadoutWarps;
     const int grid = (int)(blocks_needed < 148 * 16 ? blocks_needed : 148 * 16);
     if (wide)
-        vect ? Launch<double, true>::go(a, grid, s) : Launch<double, false>::go(a, grid, s);
+        vect ? Launch<double, true, -1>::go(a, grid, s) : Launch<double, false, -1>::go(a, grid, s);
+    else if (fix == ESA_DTYPE_F16)
+        vect ? Launch<float, true, ESA_DTYPE_F16>::go(a, grid, s) : Launch<float, false, ESA_DTYPE_F16>::go(a, grid, s);
+    else if (fix == ESA_DTYPE_BF16)
+        vect ? Launch<float, true, ESA_DTYPE_BF16>::go(a, grid, s)
+             : Launch<float, false, ESA_DTYPE_BF16>::go(a, grid, s);
     else
-        vect ? Launch<float, true>::go(a, grid, s) : Launch<float, false>::go(a, grid, s);
+        vect ? Launch<float, true, -1>::go(a, grid, s) : Launch<float, false, -1>::go(a, grid, s);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("readout launch: ") + cudaGetErrorString(e));
     return ESA_OK;
 }
 
-template <typename A, bool V>
+template <typename A, bool V, int FIX>
 struct FwdLaunch {
     static void go(const ReadoutArgs& a, int grid, cudaStream_t s) {
-        readout_fwd_kernel<A, V><<<grid, 32 * kReadoutWarps, 0, s>>>(a);
+        readout_fwd_kernel<A, V, FIX><<<grid, 32 * kReadoutWarps, 0, s>>>(a);
     }
 };
-template <typename A, bool V>
+template <typename A, bool V, int FIX>
 struct BwdLaunch {
     static void go(const ReadoutArgs& a, int grid, cudaStream_t s) {
-        readout_bwd_kernel<A, V><<<grid, 32 * kReadoutWarps, 0, s>>>(a);
+        readout_bwd_kernel<A, V, FIX><<<grid, 32 * kReadoutWarps, 0, s>>>(a);
     }
 };
+
+// The one 16-bit dtype code shared by every given code, or -1.
+int common16(std::initializer_list<int> dts) {
+    const int first = *dts.begin();
+    if (first != ESA_DTYPE_F16 && first != ESA_DTYPE_BF16) return -1;
+    for (int d : dts)
+        if (d != first) return -1;
+    return first;
+}
 
 int check_operand(const void* p, int64_t rs, int dt, int64_t C, const char* name, int* es) {
     *es = dtype_size(dt);
@@ -179,7 +212,7 @@ int readout_fwd(const void* q, int64_t qrs, int qdt, const void* E, int64_t ers,
     a.eps = eps;
     const bool wide = qdt == ESA_DTYPE_F64 || edt == ESA_DTYPE_F64 || ydt == ESA_DTYPE_F64;
     const bool vect = C % 8 == 0 && vec_ok(q, qrs, a.q.es) && vec_ok(E, ers, a.E.es) && vec_ok(y, yrs, a.y.es);
-    return readout_launch<FwdLaunch>(a, wide, vect, s);
+    return readout_launch<FwdLaunch>(a, wide, vect, common16({qdt, edt, ydt}), s);
 }
 
 int readout_bwd(const void* dy, int64_t dyrs, int dydt, const void* q, int64_t qrs, int qdt, const void* E,
@@ -208,7 +241,7 @@ int readout_bwd(const void* dy, int64_t dyrs, int dydt, const void* q, int64_t q
                       dqdt == ESA_DTYPE_F64 || dedt == ESA_DTYPE_F64;
     const bool vect = C % 8 == 0 && vec_ok(dy, dyrs, a.dy.es) && vec_ok(q, qrs, a.q.es) &&
                       vec_ok(E, ers, a.E.es) && vec_ok(dq, dqrs, a.dq.es) && vec_ok(dE, ders, a.dE.es);
-    return readout_launch<BwdLaunch>(a, wide, vect, s);
+    return readout_launch<BwdLaunch>(a, wide, vect, common16({dydt, qdt, edt, dqdt, dedt}), s);
 }
 
 }  // namespace esa
