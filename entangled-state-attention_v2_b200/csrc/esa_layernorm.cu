@@ -24,6 +24,7 @@
 // one partial row per CTA, and the partial rows are summed by a second kernel
 // in a fixed order (deterministic, no atomics).
 #include <string>
+#include <type_traits>
 
 #include "../../include/esa_b200.h"
 #include "esa_internal.h"
@@ -64,14 +65,31 @@ struct LnArgs {
     float eps;
 };
 
-template <int NCH>
+// MIX >= 0: the autocast training mix -- x, w, b (and xsum, dx, and the
+// gradient of xsum) fp32, y / dy (and res / its gradient) of the 16-bit dtype
+// code MIX -- resolved at compile time, so no load or store switches on a
+// dtype code; MIX < 0: every dtype read from the arguments at run time.
+template <int MIX>
+struct LnTypes {
+    int xdt, xes, wdt, wes, ydt, yes, rdt, res_es, dydt, dyes, dsdt, dses;
+    __device__ __forceinline__ explicit LnTypes(const LnArgs& a)
+        : xdt(MIX >= 0 ? ESA_DTYPE_F32 : a.xdt), xes(MIX >= 0 ? 4 : a.xes),
+          wdt(MIX >= 0 ? ESA_DTYPE_F32 : a.wdt), wes(MIX >= 0 ? 4 : a.wes),
+          ydt(MIX >= 0 ? MIX : a.ydt), yes(MIX >= 0 ? 2 : a.yes),
+          rdt(MIX >= 0 ? MIX : a.rdt), res_es(MIX >= 0 ? 2 : a.res_es),
+          dydt(MIX >= 0 ? MIX : a.dydt), dyes(MIX >= 0 ? 2 : a.dyes),
+          dsdt(MIX >= 0 ? ESA_DTYPE_F32 : a.dsdt), dses(MIX >= 0 ? 4 : a.dses) {}
+};
+
+template <int NCH, int MIX>
 __global__ void __launch_bounds__(32 * kLnWarps) ln_fwd_kernel(const LnArgs a) {
+    const LnTypes<MIX> ty(a);
     const int lane = threadIdx.x & 31;
     const int64_t nw = (int64_t)gridDim.x * kLnWarps;
     const float inv_c = 1.0f / float(a.C);
     for (int64_t row = (int64_t)blockIdx.x * kLnWarps + (threadIdx.x >> 5); row < a.rows; row += nw) {
-        const char* xr = a.x + row * a.C * a.xes;
-        char* yr = a.y + row * a.C * a.yes;
+        const char* xr = a.x + row * a.C * ty.xes;
+        char* yr = a.y + row * a.C * ty.yes;
         // the row stays in registers: one read of x (and res), three reductions
         float v[NCH][8];
         float s = 0.f;
@@ -79,14 +97,14 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_fwd_kernel(const LnArgs a) {
         for (int k = 0; k < NCH; ++k) {
             const int64_t c0 = lane * 8 + k * 256;
             if (c0 < a.C) {
-                load8(xr + c0 * a.xes, a.xdt, v[k]);
+                load8(xr + c0 * ty.xes, ty.xdt, v[k]);
                 if (a.res != nullptr) {
                     // xsum = x + res, rounded to x's dtype as a separate add would be
                     float u[8];
-                    load8(a.res + (row * a.C + c0) * a.res_es, a.rdt, u);
+                    load8(a.res + (row * a.C + c0) * ty.res_es, ty.rdt, u);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) v[k][i] = round_dt(v[k][i] + u[i], a.xdt);
-                    store8(a.xsum + (row * a.C + c0) * a.xes, a.xdt, v[k]);
+                    for (int i = 0; i < 8; ++i) v[k][i] = round_dt(v[k][i] + u[i], ty.xdt);
+                    store8(a.xsum + (row * a.C + c0) * ty.xes, ty.xdt, v[k]);
                 }
 #pragma unroll
                 for (int i = 0; i < 8; ++i) s += v[k][i];
@@ -110,11 +128,11 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_fwd_kernel(const LnArgs a) {
             const int64_t c0 = lane * 8 + k * 256;
             if (c0 < a.C) {
                 float w[8], bb[8], o[8];
-                load8(a.w + c0 * a.wes, a.wdt, w);
-                load8(a.b + c0 * a.wes, a.wdt, bb);
+                load8(a.w + c0 * ty.wes, ty.wdt, w);
+                load8(a.b + c0 * ty.wes, ty.wdt, bb);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) o[i] = fmaf((v[k][i] - mu) * r, w[i], bb[i]);
-                store8(yr + c0 * a.yes, a.ydt, o);
+                store8(yr + c0 * ty.yes, ty.ydt, o);
             }
         }
         if (lane == 0) {
@@ -124,9 +142,10 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_fwd_kernel(const LnArgs a) {
     }
 }
 
-template <int NCH>
+template <int NCH, int MIX>
 __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_kernel(const LnArgs a) {
     extern __shared__ float ln_smem[];  // [kLnWarps][2][C]
+    const LnTypes<MIX> ty(a);
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int64_t nw = (int64_t)gridDim.x * kLnWarps;
@@ -137,9 +156,9 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_kernel(const LnArgs a) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) dw[k][i] = db[k][i] = 0.f;
     for (int64_t row = (int64_t)blockIdx.x * kLnWarps + warp; row < a.rows; row += nw) {
-        const char* xr = a.x + row * a.C * a.xes;
-        const char* dyr = a.dy + row * a.C * a.dyes;
-        char* dxr = a.dx + row * a.C * a.xes;
+        const char* xr = a.x + row * a.C * ty.xes;
+        const char* dyr = a.dy + row * a.C * ty.dyes;
+        char* dxr = a.dx + row * a.C * ty.xes;
         const float mu = a.mean[row], r = a.rstd[row];
         float sg = 0.f, sgx = 0.f;
 #pragma unroll
@@ -147,9 +166,9 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_kernel(const LnArgs a) {
             const int64_t c0 = lane * 8 + k * 256;
             if (c0 < a.C) {
                 float v[8], d[8], w[8];
-                load8(xr + c0 * a.xes, a.xdt, v);
-                load8(dyr + c0 * a.dyes, a.dydt, d);
-                load8(a.w + c0 * a.wes, a.wdt, w);
+                load8(xr + c0 * ty.xes, ty.xdt, v);
+                load8(dyr + c0 * ty.dyes, ty.dydt, d);
+                load8(a.w + c0 * ty.wes, ty.wdt, w);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const float xh = (v[i] - mu) * r;
@@ -167,9 +186,9 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_kernel(const LnArgs a) {
             const int64_t c0 = lane * 8 + k * 256;
             if (c0 < a.C) {
                 float v[8], d[8], w[8], o[8];
-                load8(xr + c0 * a.xes, a.xdt, v);
-                load8(dyr + c0 * a.dyes, a.dydt, d);
-                load8(a.w + c0 * a.wes, a.wdt, w);
+                load8(xr + c0 * ty.xes, ty.xdt, v);
+                load8(dyr + c0 * ty.dyes, ty.dydt, d);
+                load8(a.w + c0 * ty.wes, ty.wdt, w);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const float xh = (v[i] - mu) * r;
@@ -177,12 +196,12 @@ __global__ void __launch_bounds__(32 * kLnWarps) ln_bwd_kernel(const LnArgs a) {
                 }
                 if (a.dsum != nullptr) {
                     float ds[8];
-                    load8(a.dsum + (row * a.C + c0) * a.dses, a.dsdt, ds);
+                    load8(a.dsum + (row * a.C + c0) * ty.dses, ty.dsdt, ds);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) o[i] += ds[i];
                 }
-                store8(dxr + c0 * a.xes, a.xdt, o);
-                if (a.dres != nullptr) store8(a.dres + (row * a.C + c0) * a.res_es, a.rdt, o);
+                store8(dxr + c0 * ty.xes, ty.xdt, o);
+                if (a.dres != nullptr) store8(a.dres + (row * a.C + c0) * ty.res_es, ty.rdt, o);
             }
         }
     }
@@ -232,6 +251,24 @@ __global__ void __launch_bounds__(256) ln_bwd_finalize_kernel(const float* __res
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool is16(int dt) { return dt == ESA_DTYPE_F16 || dt == ESA_DTYPE_BF16; }
+
+// Calls f(std::integral_constant<int, n>) for n = 1..kLnMaxChunks (8-channel
+// chunks per lane).
+template <typename F>
+void with_nch(int64_t n, F&& f) {
+    switch (n) {
+        case 1: f(std::integral_constant<int, 1>{}); break;
+        case 2: f(std::integral_constant<int, 2>{}); break;
+        case 3: f(std::integral_constant<int, 3>{}); break;
+        case 4: f(std::integral_constant<int, 4>{}); break;
+        case 5: f(std::integral_constant<int, 5>{}); break;
+        case 6: f(std::integral_constant<int, 6>{}); break;
+        case 7: f(std::integral_constant<int, 7>{}); break;
+        default: f(std::integral_constant<int, 8>{}); break;
+    }
+}
 
 int ln_check(const void* p, int dt, int64_t C, const char* name, int* es) {
     *es = dtype_size(dt);
@@ -292,16 +329,19 @@ int layer_norm_fwd(const void* x, int xdt, const void* res, int rdt, void* xsum,
     a.C = C;
     a.eps = (float)eps;
     const int grid = ln_grid(rows);
-    switch ((C + 255) / 256) {
-        case 1: ln_fwd_kernel<1><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
-        case 2: ln_fwd_kernel<2><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
-        case 3: ln_fwd_kernel<3><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
-        case 4: ln_fwd_kernel<4><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
-        case 5: ln_fwd_kernel<5><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
-        case 6: ln_fwd_kernel<6><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
-        case 7: ln_fwd_kernel<7><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
-        default: ln_fwd_kernel<8><<<grid, 32 * kLnWarps, 0, s>>>(a); break;
-    }
+    // the autocast training mix (fp32 stream and weights, 16-bit output and residual)
+    const int mix = (xdt == ESA_DTYPE_F32 && wdt == ESA_DTYPE_F32 && is16(ydt) && (res == nullptr || rdt == ydt))
+                        ? ydt : -1;
+    auto launch = [&](auto nch_tag) {
+        constexpr int NCH = decltype(nch_tag)::value;
+        if (mix == ESA_DTYPE_F16)
+            ln_fwd_kernel<NCH, ESA_DTYPE_F16><<<grid, 32 * kLnWarps, 0, s>>>(a);
+        else if (mix == ESA_DTYPE_BF16)
+            ln_fwd_kernel<NCH, ESA_DTYPE_BF16><<<grid, 32 * kLnWarps, 0, s>>>(a);
+        else
+            ln_fwd_kernel<NCH, -1><<<grid, 32 * kLnWarps, 0, s>>>(a);
+    };
+    with_nch((C + 255) / 256, launch);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("layer norm launch: ") + cudaGetErrorString(e));
     return ESA_OK;
@@ -347,20 +387,25 @@ int layer_norm_bwd(const void* dy, int dydt, const void* dsum, int dsdt, const v
     const size_t smem = (size_t)kLnWarps * 2 * C * sizeof(float);
     const int nch = (int)((C + 255) / 256);
     cudaError_t e = cudaSuccess;
-    auto launch = [&](auto kernel) {
+    auto launch1 = [&](auto kernel) {
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e == cudaSuccess) kernel<<<grid, 32 * kLnWarps, smem, s>>>(a);
     };
-    switch (nch) {
-        case 1: launch(ln_bwd_kernel<1>); break;
-        case 2: launch(ln_bwd_kernel<2>); break;
-        case 3: launch(ln_bwd_kernel<3>); break;
-        case 4: launch(ln_bwd_kernel<4>); break;
-        case 5: launch(ln_bwd_kernel<5>); break;
-        case 6: launch(ln_bwd_kernel<6>); break;
-        case 7: launch(ln_bwd_kernel<7>); break;
-        default: launch(ln_bwd_kernel<8>); break;
-    }
+    // the autocast training mix: fp32 stream, weights and xsum gradient,
+    // 16-bit dy and residual gradient
+    const int mix = (xdt == ESA_DTYPE_F32 && wdt == ESA_DTYPE_F32 && is16(dydt) &&
+                     (dsum == nullptr || dsdt == ESA_DTYPE_F32) && (dres == nullptr || rdt == dydt))
+                        ? dydt : -1;
+    auto launch = [&](auto nch_tag) {
+        constexpr int NCH = decltype(nch_tag)::value;
+        if (mix == ESA_DTYPE_F16)
+            launch1(ln_bwd_kernel<NCH, ESA_DTYPE_F16>);
+        else if (mix == ESA_DTYPE_BF16)
+            launch1(ln_bwd_kernel<NCH, ESA_DTYPE_BF16>);
+        else
+            launch1(ln_bwd_kernel<NCH, -1>);
+    };
+    with_nch(nch, launch);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e == cudaSuccess) {
         ln_bwd_finalize_kernel<<<(unsigned)((2 * C + 31) / 32), dim3(32, 8), 0, s>>>(
