@@ -52,6 +52,22 @@ ESA_EXPORT const char* esa_last_error(void) { return t_last_error.c_str(); }
 
 ESA_EXPORT int esa_scan_last_path(void) { return last_scan_path(); }
 
+ESA_EXPORT int esa_cross_entropy_fwd(const void* logits, int64_t row_stride, int dtype, const int64_t* targets,
+                                     int64_t ignore_index, float* lse, float* loss, int64_t rows, int64_t V,
+                                     void* stream) {
+    clear_error();
+    return cross_entropy_fwd(logits, row_stride, dtype, targets, ignore_index, lse, loss, rows, V,
+                             static_cast<cudaStream_t>(stream));
+}
+
+ESA_EXPORT int esa_cross_entropy_bwd(const void* logits, int64_t row_stride, int dtype, const int64_t* targets,
+                                     int64_t ignore_index, const float* lse, const float* grad_rows, void* dlogits,
+                                     int64_t dlogits_row_stride, int64_t rows, int64_t V, void* stream) {
+    clear_error();
+    return cross_entropy_bwd(logits, row_stride, dtype, targets, ignore_index, lse, grad_rows, dlogits,
+                             dlogits_row_stride, rows, V, static_cast<cudaStream_t>(stream));
+}
+
 ESA_EXPORT int esa_readout_fwd(const void* q, int64_t q_row_stride, int q_dtype, const void* E,
                                int64_t e_row_stride, int e_dtype, void* y, int64_t y_row_stride,
                                int y_dtype, void* rstd, int64_t rows, int64_t C, double eps,

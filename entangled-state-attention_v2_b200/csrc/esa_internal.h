@@ -125,6 +125,11 @@ int readout_fwd(const void* q, int64_t qrs, int qdt, const void* E, int64_t ers,
 int readout_bwd(const void* dy, int64_t dyrs, int dydt, const void* q, int64_t qrs, int qdt, const void* E,
                 int64_t ers, int edt, const void* rstd, void* dq, int64_t dqrs, int dqdt, void* dE,
                 int64_t ders, int dedt, int64_t rows, int64_t C, double eps, cudaStream_t s);
+int cross_entropy_fwd(const void* logits, int64_t ld, int dtype, const int64_t* targets, int64_t ignore_index,
+                      float* lse, float* loss, int64_t rows, int64_t V, cudaStream_t s);
+int cross_entropy_bwd(const void* logits, int64_t ld, int dtype, const int64_t* targets, int64_t ignore_index,
+                      const float* lse, const float* grad_rows, void* dlogits, int64_t dld, int64_t rows, int64_t V,
+                      cudaStream_t s);
 int lightning_step(const void* qgv, int64_t qrs, int qdt, const void* state, void* new_state,
                    int sdt, void* z, int zdt, int64_t nb, int64_t C, double gmin, double gmax,
                    double eps, cudaStream_t s);

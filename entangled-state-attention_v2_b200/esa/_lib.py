@@ -49,6 +49,8 @@ SIGNATURES = {
                                       _vp, _vp, _vp, _sz, _i64, _i64, _vp]),
     "esa_layer_norm_bwd": (_int, [_vp, _int, _vp, _int, _vp, _int, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _i64,
                                   _i64, _vp]),
+    "esa_cross_entropy_fwd": (_int, [_vp, _i64, _int, _vp, _i64, _vp, _vp, _i64, _i64, _vp]),
+    "esa_cross_entropy_bwd": (_int, [_vp, _i64, _int, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "esa_wait_selftest": (_int, [ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_uint), _vp]),
     "esa_scan_workspace_bytes": (_sz, [_i64, _i64, _i64, _int, _int]),
     "esa_scan_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _sz, _vp]),

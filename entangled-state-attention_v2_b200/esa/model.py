@@ -272,8 +272,13 @@ class ESAModel(nn.Module):
         logits = self.lm_head(h)
         loss = None
         if targets is not None:
-            loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1),
-                                   ignore_index=-1)
+            flat, tflat = logits.reshape(-1, logits.size(-1)), targets.reshape(-1)
+            if ops.cross_entropy_supported(flat, tflat):
+                # fused LM-head loss: reads the 16-bit logits twice in all,
+                # instead of an fp32 copy, an fp32 log-softmax and their backward
+                loss = ops.cross_entropy(flat, tflat, ignore_index=-1)
+            else:
+                loss = F.cross_entropy(flat, tflat, ignore_index=-1)
         return logits, loss
 
     def compile_training(self, *, mode: str | None = None, fullgraph: bool | None = None) -> "ESAModel":

@@ -659,3 +659,84 @@ def _add_ln_bwd(ctx, dsum, dy, dmean_unused, drstd_unused):
 
 
 torch.library.register_autograd("esa_b200::add_layer_norm", _add_ln_bwd, setup_context=_add_ln_setup)
+
+
+# ---------------------------------------------------------------------------
+# Cross-entropy of the LM head (the ESAModel training loss)
+# ---------------------------------------------------------------------------
+def cross_entropy_supported(logits: Tensor, targets: Tensor) -> bool:
+    """The fused loss takes 2-D CUDA logits (f16, bf16, f32) and int64 targets."""
+    return (logits.is_cuda and logits.dim() == 2 and logits.dtype in (torch.float16, torch.bfloat16, torch.float32)
+            and targets.dtype == torch.int64 and targets.dim() == 1 and targets.shape[0] == logits.shape[0]
+            and logits.stride(1) == 1)
+
+
+@torch.library.custom_op("esa_b200::cross_entropy_rows", mutates_args=())
+def cross_entropy_rows(logits: Tensor, targets: Tensor, ignore_index: int) -> tuple[Tensor, Tensor]:
+    """(loss, lse) per row of logits [rows, V]: lse = logsumexp, loss = lse -
+    logits[target] (0 on ignored rows), both fp32; one read of the logits."""
+    _require_cuda("esa cross entropy", logits, targets)
+    rows, V = logits.shape
+    tc = targets.contiguous()
+    loss = torch.empty(rows, dtype=torch.float32, device=logits.device)
+    lse = torch.empty(rows, dtype=torch.float32, device=logits.device)
+    if rows == 0:
+        return loss, lse
+    _lib.check(_lib.lib().esa_cross_entropy_fwd(logits.data_ptr(), logits.stride(0), dtype_code(logits.dtype),
+                                                tc.data_ptr(), int(ignore_index), lse.data_ptr(), loss.data_ptr(),
+                                                rows, V, _stream(logits)), "esa_cross_entropy_fwd")
+    return loss, lse
+
+
+@cross_entropy_rows.register_fake
+def _(logits, targets, ignore_index):
+    rows = logits.shape[0]
+    return logits.new_empty(rows, dtype=torch.float32), logits.new_empty(rows, dtype=torch.float32)
+
+
+@torch.library.custom_op("esa_b200::cross_entropy_rows_backward", mutates_args=())
+def cross_entropy_rows_backward(logits: Tensor, targets: Tensor, lse: Tensor, grad_rows: Tensor,
+                                ignore_index: int) -> Tensor:
+    """d logits (logits' dtype) = grad_rows[i] (softmax(logits[i]) - onehot(target[i])), 0 on ignored rows."""
+    _require_cuda("esa cross entropy backward", logits, targets, lse, grad_rows)
+    rows, V = logits.shape
+    dz = torch.empty((rows, V), dtype=logits.dtype, device=logits.device)
+    if rows == 0:
+        return dz
+    g = grad_rows.to(torch.float32).contiguous()
+    _lib.check(_lib.lib().esa_cross_entropy_bwd(logits.data_ptr(), logits.stride(0), dtype_code(logits.dtype),
+                                                targets.contiguous().data_ptr(), int(ignore_index), lse.data_ptr(),
+                                                g.data_ptr(), dz.data_ptr(), V, rows, V, _stream(logits)),
+               "esa_cross_entropy_bwd")
+    return dz
+
+
+@cross_entropy_rows_backward.register_fake
+def _(logits, targets, lse, grad_rows, ignore_index):
+    return torch.empty_like(logits)
+
+
+def _xent_setup(ctx, inputs, output):
+    logits, targets, ignore_index = inputs
+    _, lse = output
+    ctx.ignore_index = ignore_index
+    ctx.save_for_backward(logits, targets, lse)
+
+
+def _xent_bwd(ctx, dloss, dlse_unused):
+    logits, targets, lse = ctx.saved_tensors
+    if dloss is None:
+        return None, None, None
+    return cross_entropy_rows_backward(logits, targets, lse, dloss, ctx.ignore_index), None, None
+
+
+torch.library.register_autograd("esa_b200::cross_entropy_rows", _xent_bwd, setup_context=_xent_setup)
+
+
+def cross_entropy(logits: Tensor, targets: Tensor, ignore_index: int = -100) -> Tensor:
+    """Mean cross-entropy over the rows whose target is not ignore_index, as
+    `F.cross_entropy(logits, targets, ignore_index=...)` computes it (fp32
+    arithmetic whatever the logits' dtype; NaN when every row is ignored)."""
+    loss_rows, _ = cross_entropy_rows(logits, targets, ignore_index)
+    count = (targets != ignore_index).sum()
+    return loss_rows.sum() / count

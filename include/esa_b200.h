@@ -125,6 +125,27 @@ int esa_add_layer_norm_bwd(const void *dy, int dy_dtype, const void *dsum, int d
  * a hang.  No reference counterpart. */
 int esa_wait_selftest(unsigned int *completed, unsigned int *waited_ms, void *stream);
 
+/* Cross-entropy of the LM head (the ESAModel training loss), forward.
+ * Replaces `F.cross_entropy(logits.reshape(-1, V), targets, ignore_index=-1)`
+ * of the reference's esa/model.py (ESAModel.forward) up to its mean: for each
+ * row i of logits [rows, V] (row stride `row_stride` elements; f16, bf16 or
+ * f32), lse[i] = log sum_j exp(logits[i, j]) and loss[i] = lse[i] -
+ * logits[i, targets[i]] (fp32; 0 where targets[i] == ignore_index, NaN where a
+ * target is out of [0, V)).  The caller averages loss over the rows that are
+ * not ignored.  Reads the logits once; lse is kept for the backward. */
+int esa_cross_entropy_fwd(const void *logits, int64_t row_stride, int dtype, const int64_t *targets,
+                          int64_t ignore_index, float *lse, float *loss, int64_t rows, int64_t V,
+                          void *stream);
+
+/* Gradient of esa_cross_entropy_fwd: dlogits[i, j] = grad_rows[i] *
+ * (exp(logits[i, j] - lse[i]) - [j == targets[i]]), zero on ignored rows,
+ * written in the logits' dtype (row stride `dlogits_row_stride`).  grad_rows:
+ * fp32 [rows], the gradient of the loss w.r.t. each row's loss[i] (for a mean
+ * over n rows: the upstream gradient / n). */
+int esa_cross_entropy_bwd(const void *logits, int64_t row_stride, int dtype, const int64_t *targets,
+                          int64_t ignore_index, const float *lse, const float *grad_rows, void *dlogits,
+                          int64_t dlogits_row_stride, int64_t rows, int64_t V, void *stream);
+
 /* Kernel family of the last scan launch on this host thread (diagnostics and
  * tests): ESA_PATH_NONE before any, ESA_PATH_SEQUENTIAL (one thread per
  * channel, any alignment), ESA_PATH_LOOKBACK (time chunks, decoupled

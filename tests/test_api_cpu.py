@@ -27,7 +27,7 @@ def test_header_declares_the_abi():
         "esa_scan_host_staging_bytes", "esa_scan_fwd_host", "esa_scan_fwd_resume",
         "esa_wait_selftest", "esa_readout_fwd", "esa_readout_bwd", "esa_layer_norm_fwd",
         "esa_layer_norm_workspace_bytes", "esa_layer_norm_bwd", "esa_add_layer_norm_fwd",
-        "esa_add_layer_norm_bwd"}
+        "esa_add_layer_norm_bwd", "esa_cross_entropy_fwd", "esa_cross_entropy_bwd"}
 
 
 def test_library_loads_and_exports_every_declared_symbol():
