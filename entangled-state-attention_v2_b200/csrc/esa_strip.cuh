@@ -130,18 +130,8 @@ __device__ __forceinline__ void sts_planar(A* row, int cl, const A (&in)[N]) {
     }
 }
 
-// Resident CTAs per SM the register budget is cut for: three for the fused
-// gated reverse's narrowest strips (32-channel strips of few-channel layers:
-// the ESAModel's [16,2048,768] then runs 384 strips in one wave, 135.6 vs
-// 141.7 us with 64-channel strips; the gated forward measured no gain, 116.6
-// vs 114.7 us, and keeps its budget), two otherwise.
-template <Kind K, typename Tin, typename Te, int LPR>
-constexpr int strip_min_ctas() {
-    return (K == Kind::RevGated && LPR == 4) ? 3 : 2;
-}
-
 template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM_>
-__global__ void __launch_bounds__(256, strip_min_ctas<K, Tin, Te, LPR>()) strip_scan_kernel(const StripParams prm,
+__global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams prm,
                                                          const __grid_constant__ CUtensorMap m0,
                                                          const __grid_constant__ CUtensorMap m1,
                                                          const __grid_constant__ CUtensorMap m2,
