@@ -10,6 +10,10 @@ inputs, so that a profiler can skip the first launches and capture one:
                split scan: summary pass, piece composition, output pass)
     readout    layer core forward + backward (readout kernels), [16,2048,768]
     layernorm  fused LayerNorm forward + backward, [16,2048,768] fp32 -> fp16
+    train      the ESAModel training step (12 layers of 768, batch 16 x 2048,
+               fp16 autocast, AdamW): four warm-up steps, then two steps under
+               torch.profiler; prints the device time per step of the top
+               kernels
 """
 
 from __future__ import annotations
@@ -20,12 +24,50 @@ import torch
 
 from . import ops
 
-WORKLOADS = ("rev", "gated", "split", "readout", "layernorm")
+WORKLOADS = ("rev", "gated", "split", "readout", "layernorm", "train")
+
+
+def train_profile(top: int = 30) -> None:
+    from torch.profiler import ProfilerActivity, profile
+
+    from .model import ESAModel, ESAModelConfig
+    torch.manual_seed(1234)
+    cfg = ESAModelConfig(vocab_size=32000, block=2048, n_layer=12, head=12, embd=768, backend="thunder",
+                         precision="fp16", dropout=0.0, bias=True, tie_embeddings=True, training_compile=False)
+    model = ESAModel(cfg, device="cuda")
+    model.train()
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, fused=True)
+    scaler = torch.amp.GradScaler("cuda")
+    ids = torch.randint(0, 32000, (16, 2049), device="cuda")
+
+    def step():
+        with torch.autocast("cuda", dtype=torch.float16):
+            _, loss = model(ids[:, :-1], ids[:, 1:])
+        scaler.scale(loss).backward()
+        scaler.step(opt)
+        scaler.update()
+        opt.zero_grad(set_to_none=True)
+
+    for _ in range(4):
+        step()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+    rows = sorted(((k.device_time_total, k.count, k.key) for k in prof.key_averages()), reverse=True)
+    total = sum(r[0] for r in rows)
+    print(f"device time per step: {total / 2:.1f} us")
+    for t, n, key in rows[:top]:
+        print(f"{t / 2:10.1f} us {100 * t / total:5.1f} % {n // 2:4d} launches  {key[:100]}")
 
 
 def run(name: str, iters: int = 4) -> None:
     if name not in WORKLOADS:
         raise ValueError(f"unknown workload {name!r}; one of {WORKLOADS}")
+    if name == "train":
+        train_profile()
+        return
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
 
