@@ -75,6 +75,28 @@ def test_abi_argument_errors_need_no_gpu():
     assert rc == -1 and "stride" in _lib.last_error()
 
 
+def test_cross_entropy_argument_errors_need_no_gpu():
+    """The LM-head loss entry points reject bad shapes and dtypes before any
+    device work; the Python op only takes 2-D CUDA logits."""
+    import torch
+    from esa import _lib, ops
+    L = _lib.lib()
+    rc = L.esa_cross_entropy_fwd(None, 10, _lib.DTYPE_F16, None, -1, None, None, 4, 0, None)
+    assert rc == -1 and "V > 0" in _lib.last_error()
+    rc = L.esa_cross_entropy_fwd(None, 5, _lib.DTYPE_F16, None, -1, None, None, 4, 10, None)
+    assert rc == -1 and "row stride" in _lib.last_error()
+    rc = L.esa_cross_entropy_fwd(None, 10, _lib.DTYPE_F64, None, -1, None, None, 4, 10, None)
+    assert rc == -2
+    rc = L.esa_cross_entropy_bwd(None, 10, _lib.DTYPE_F16, None, -1, None, None, None, 8, 4, 10, None)
+    assert rc == -1 and "gradient row stride" in _lib.last_error()
+    rc = L.esa_cross_entropy_fwd(None, 10, _lib.DTYPE_F32, None, -1, None, None, 4, 10, None)
+    assert rc == -1 and "null" in _lib.last_error()
+    z = torch.randn(4, 10)
+    t = torch.zeros(4, dtype=torch.int64)
+    assert not ops.cross_entropy_supported(z, t)          # CPU logits: the model keeps F.cross_entropy
+    assert not ops.cross_entropy_supported(z[None], t)    # 3-D
+
+
 def test_public_surface_matches_reference():
     import esa
     from esa import ESA
