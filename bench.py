@@ -454,6 +454,38 @@ def _bf16_peak():
     return 1400.0, "fallback"
 
 
+def _in_situ_scan(step, dev, n_elem: int, n_layer: int) -> dict | None:
+    """GB/s of the fused gated scans inside the training step: one extra step
+    after the timed region under torch.profiler (CUDA activity), the device
+    time of the forward and reverse scan kernels against their algorithmic
+    bytes (forward reads g, v and writes E: 3 x 2 bytes an element; reverse
+    reads g, v, E, dE and writes dg, dv: 6 x 2 bytes)."""
+    import torch
+    try:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize(dev)
+        fwd = bwd = 0.0
+        for k in prof.key_averages():
+            name = k.key
+            if "scan_kernel" not in name:
+                continue
+            if "Kind)1" in name:
+                fwd += k.device_time_total
+            elif "Kind)3" in name:
+                bwd += k.device_time_total
+        if fwd <= 0 or bwd <= 0:
+            return None
+        hbm, _ = _peaks()
+        f = n_layer * 3 * n_elem * 2 / (fwd * 1e-6) / 1e9
+        b = n_layer * 6 * n_elem * 2 / (bwd * 1e-6) / 1e9
+        return {"fwd_GBps": f, "bwd_GBps": b, "fwd_frac": f / hbm, "bwd_frac": b / hbm, "unit": "GB/s",
+                "source": "torch.profiler device time of one step after the timed region"}
+    except Exception as exc:  # the extra figure never blocks the bench line
+        return {"error": str(exc)}
+
+
 def run_train(args) -> None:
     import datetime
 
@@ -520,6 +552,7 @@ def run_train(args) -> None:
     ops.check_device_status(dev)
     tok = ws * B * T * args.steps / (ms * 1e-3)
     peak, kind = _bf16_peak()
+    scan = _in_situ_scan(step, dev, B * T * cfg.embd, cfg.n_layer)
     flops_per_token = 6 * n_params
     if rank == 0:
         line = {
@@ -534,6 +567,7 @@ def run_train(args) -> None:
             "roofline": {"bound": "tensor", "achieved": tok * flops_per_token / 1e12, "peak": peak,
                          "unit": "TFLOP/s", "frac": tok * flops_per_token / 1e12 / peak,
                          "peak_kind": kind, "flops_per_token": flops_per_token},
+            "in_situ_scan": scan,
             "e2e": {"value": tok, "unit": "tokens/s", "h2d_bytes_per_step": host_ids.numel() * 8,
                     "d2h_bytes_per_step": 4},
             "clocks": clk,
