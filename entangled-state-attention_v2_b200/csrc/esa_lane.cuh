@@ -330,8 +330,9 @@ int lane_launch_kind(const ScanCall& call, bool* taken, double min_warps_per_sm)
     // two consumer warps (256-byte rows) when every SM still gets a CTA
     // (fp16 forward, us: [32,4096,16,64] 132.8 vs 134.3 with one warp;
     // [74,2048,16,64] 158.2 vs 180.0; [128,1024,16,64] 138.0 vs 154.1)
-    int nw = force_nw ? force_nw : 1;
-    if (!force_nw) {
+    // an override other than 1 or 2 falls back to the automatic choice
+    int nw = (force_nw == 1 || force_nw == 2) ? force_nw : 1;
+    if (force_nw != 1 && force_nw != 2) {
         using C2 = LaneCfg<K, Tin, Te, 2>;
         const int64_t ctas2 = nb * ((hd + C2::WS - 1) / C2::WS);
         nw = ctas2 >= (int64_t)sms ? 2 : 1;
