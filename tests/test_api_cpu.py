@@ -209,6 +209,12 @@ def test_fake_kernels_trace_without_gpu():
                                torch.empty(3, 32, device="meta", dtype=torch.float16),
                                0.8, 0.995, 1e-5, torch.float32)
     assert ns.dtype == torch.float16 and z.dtype == torch.float32 and z.shape == (3, 32)
+    z = torch.empty(6, 50, device="meta", dtype=torch.float16)
+    t = torch.empty(6, device="meta", dtype=torch.int64)
+    loss, lse = ops.cross_entropy_rows(z, t, -1)
+    assert loss.shape == (6,) and lse.shape == (6,) and loss.dtype == torch.float32
+    dz = ops.cross_entropy_rows_backward(z, t, lse, loss, -1)
+    assert dz.shape == z.shape and dz.dtype == torch.float16
 
 
 def test_library_symbols_via_ctypes_cdll():
