@@ -7,7 +7,7 @@ slices only through one state per channel, so the exchange is tiny:
   1. summary (local, reads A and B once):  E_end_r (from a zero state) and
      P_r = prod_t A_t over the slice -- ``esa_scan_summary``;
   2. exchange: all-gather of the [2, B, H*D] fp32 summaries (NCCL; 64 KB per
-     rank for B=4, H*D=2048);
+     rank for B=4, H*D=2048; a gloo group exchanges them through host memory);
   3. carry: C_0 = e0 (or 0), C_{r+1} = P_r * C_r + E_end_r, composed in rank
      order on every rank (the same arithmetic everywhere: deterministic);
   4. scan (local): the slice's outputs from its exact incoming state C_r.
@@ -77,8 +77,16 @@ def sequence_parallel_scan(A: torch.Tensor, B: torch.Tensor, *, group=None, comp
                                       e_end.data_ptr(), prod.data_ptr(), ws.data_ptr(), ws.numel(),
                                       stream), "esa_scan_summary")
     mine = torch.stack([e_end, prod])
-    gathered = [torch.empty_like(mine) for _ in range(world)]
-    dist.all_gather(gathered, mine, group=group)
+    if dist.get_backend(group) == "gloo":
+        # gloo gathers host tensors: the 2*B*H*D summaries cross to the host
+        # and back (ranks that share one GPU, or no NVLink)
+        host = mine.cpu()
+        gathered = [torch.empty_like(host) for _ in range(world)]
+        dist.all_gather(gathered, host, group=group)
+        gathered = [t.to(A.device) for t in gathered]
+    else:
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine, group=group)
     carry = compose_carries(gathered, rank, e0).contiguous()
     E = torch.empty_like(A)
     if T > 0 and hd > 0 and nb > 0:

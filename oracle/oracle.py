@@ -240,3 +240,30 @@ def thunder_scan_port(A: torch.Tensor, B: torch.Tensor, compass: int = 16) -> to
     incoming[:, 1:] = cb[:, :-1]
     E = (loc + prod * incoming.unsqueeze(2)).reshape(nb, G * compass, H, D)
     return E[:, :T]
+
+
+def pulse_scan_port(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
+    """Torch restatement of the reference's sequential scan (pulse.py:12-31):
+    one state update per step in the input dtype, the steps stacked along T.
+    Differentiable through torch autograd, as the reference's is."""
+    state = torch.zeros_like(A[:, 0])
+    outs = []
+    for t in range(A.shape[1]):
+        state = A[:, t] * state + B[:, t]
+        outs.append(state)
+    return torch.stack(outs, dim=1)
+
+
+def pulse_layer_port(x, qgv_w, out_w, head, *, gmin=0.80, gmax=0.995, eps=1e-5):
+    """Torch restatement of PulseESA.forward (pulse.py:69-98) in the input
+    dtype with the sequential scan of ``pulse_scan_port``: the reference's CPU
+    layer (the timed CPU baseline of the layer workload)."""
+    Bsz, T, C = x.shape
+    D = C // head
+    qgv = x @ qgv_w.t()
+    q, g, v = qgv.split(C, dim=-1)
+    A = gmin + (gmax - gmin) * torch.sigmoid(g)
+    Bw = (1.0 - A) * torch.tanh(v)
+    E = pulse_scan_port(A.reshape(Bsz, T, head, D), Bw.reshape(Bsz, T, head, D)).reshape(Bsz, T, C)
+    E = E * torch.rsqrt(E.pow(2).mean(dim=-1, keepdim=True) + eps)
+    return (torch.sigmoid(q) * E) @ out_w.t()

@@ -29,6 +29,19 @@ Fixtures produced (all small enough for git):
 * ``model_generate.npz``   -- a tiny ESAModel (2 layers, embd 32, head 4, vocab
   64, fp32, backend thunder) state_dict, a prompt, and greedy generate ids with
   prefill "thunder_16" and "pulse" (compile=False).
+* ``model_decode_24l.npz`` -- the decode workload's model (24 layers, embd 1024,
+  head 16, vocab 32000, block 1024, fp32, backend thunder) filled with the
+  seeded weights of ``seeded.py`` (not stored: 1.3 GB); a 512-token uniform
+  prompt and the 256 greedy ids of ``generate(prefill="thunder_16",
+  runtime="lightning", temperature=0, compile=False)``, plus the smallest
+  top-1/top-2 logit gap of a teacher-forced pass over the result (how far the
+  greedy choices are from a tie).
+* ``model_train_step.npz`` -- a small fp32 ESAModel (2 layers, embd 64, head 4,
+  vocab 256, block 512, seeded weights) on a [12, 512] batch (6144 rows): the
+  training loss, a slice of the logits and the gradient of every parameter
+  after ``loss.backward()``.
+
+Only some fixtures: ``python tests/golden/make_golden.py decode_24l train_step``.
 """
 
 from __future__ import annotations
@@ -40,7 +53,6 @@ from pathlib import Path
 import numpy as np
 import torch
 
-REF = os.environ.get("ESA_REFERENCE_PATH", "/root/reference")
 OUT = Path(__file__).resolve().parent
 
 
@@ -53,14 +65,26 @@ def _np(t: torch.Tensor) -> np.ndarray:
 
 
 def main() -> None:
-    sys.path.insert(0, REF)
+    ref = os.environ.get("ESA_REFERENCE_PATH")
+    if not ref:
+        raise SystemExit("set ESA_REFERENCE_PATH to the reference checkout (the directory holding esa/)")
+    only = set(sys.argv[1:])
+    sys.path.insert(0, ref)
+    sys.path.insert(0, str(OUT))
     import esa  # noqa: F401  (the reference package)
     from esa import ESA, ESAModel, ESAModelConfig
     from esa.backends.pulse import pulse_scan
     from esa.backends.thunder import thunder_scan
 
-    assert "reference" in esa.__file__ or REF in esa.__file__, esa.__file__
+    assert esa.__file__.startswith(os.path.abspath(ref)), esa.__file__
     torch.set_num_threads(min(8, os.cpu_count() or 1))
+    if only:
+        unknown = only - set(MODEL_FIXTURES)
+        if unknown:
+            raise SystemExit(f"unknown fixtures {sorted(unknown)}; choose from {sorted(MODEL_FIXTURES)}")
+        for name in sorted(only):
+            MODEL_FIXTURES[name]()
+        return
 
     # 1. The reference's own chunked-scan parity case.
     torch.manual_seed(1)
@@ -178,7 +202,54 @@ def main() -> None:
         ids=_np(ids), logits=_np(logits), **gen,
         **{f"sd::{k}": _np(v) for k, v in sd.items()},
     )
+    for fn in MODEL_FIXTURES.values():
+        fn()
     print("fixtures written to", OUT)
+
+
+def decode_24l() -> None:
+    """Greedy ids of the 24-layer decode model (fp32) on seeded weights."""
+    from esa import ESAModel, ESAModelConfig
+    from seeded import fill_model
+
+    cfg = ESAModelConfig(vocab_size=32000, block=1024, n_layer=24, head=16, embd=1024,
+                         dropout=0.0, precision="fp32", backend="thunder")
+    model = ESAModel(cfg, device="cpu")
+    fill_model(model, seed=24, n_layer=cfg.n_layer)
+    model.eval()
+    ids = torch.from_numpy(np.random.Generator(np.random.PCG64(512)).integers(0, 32000, size=(1, 512)))
+    seq = model.generate(input_ids=ids, seek=256, prefill="thunder_16", runtime="lightning",
+                         temperature=0.0, compile=False)
+    with torch.no_grad():
+        logits, _ = model(seq[:, :-1])
+    top2 = torch.topk(logits[0, 511:], 2, dim=-1).values
+    gap = (top2[:, 0] - top2[:, 1]).min()
+    np.savez_compressed(OUT / "model_decode_24l.npz", prompt=_np(ids), seq=_np(seq),
+                        min_top2_gap=np.float32(gap.item()), weight_seed=np.int64(24))
+    print("decode_24l: min top-2 logit gap", float(gap))
+
+
+def train_step() -> None:
+    """Loss, logits and parameter gradients of one fp32 ESAModel training step."""
+    from esa import ESAModel, ESAModelConfig
+    from seeded import fill_model
+
+    cfg = ESAModelConfig(vocab_size=256, block=512, n_layer=2, head=4, embd=64, dropout=0.0,
+                         precision="fp32", backend="thunder", training_compile=False)
+    model = ESAModel(cfg, device="cpu")
+    fill_model(model, seed=7, n_layer=cfg.n_layer)
+    model.train()
+    ids = torch.from_numpy(np.random.Generator(np.random.PCG64(513)).integers(0, 256, size=(12, 513)))
+    logits, loss = model(ids[:, :-1], ids[:, 1:])
+    loss.backward()
+    out = {"ids": _np(ids), "loss": _np(loss), "logits_rows_0_5_t_0_64": _np(logits[[0, 5], :64])}
+    for name, p in model.named_parameters():
+        out[f"grad::{name}"] = _np(p.grad)
+    np.savez_compressed(OUT / "model_train_step.npz", **out)
+    print("train_step: loss", float(loss.detach()))
+
+
+MODEL_FIXTURES = {"decode_24l": decode_24l, "train_step": train_step}
 
 
 if __name__ == "__main__":

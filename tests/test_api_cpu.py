@@ -222,3 +222,30 @@ def test_library_symbols_via_ctypes_cdll():
     cdll = ctypes.CDLL(str(_lib.LIB_PATH))
     for name in _declared_symbols():
         getattr(cdll, name)
+
+
+def test_seeded_weights_cover_the_model_fixtures():
+    """The model-level fixtures carry no weights: both sides fill the model
+    with tests/golden/seeded.py.  Its values are deterministic, the tied
+    wte / lm_head weight is filled once, and this package's ESAModel has the
+    parameter set the training-step fixture's gradients were taken over."""
+    import sys
+
+    import numpy as np
+    from conftest import GOLDEN
+    from esa import ESAModel, ESAModelConfig
+    if str(GOLDEN) not in sys.path:
+        sys.path.insert(0, str(GOLDEN))
+    from seeded import fill_model
+    cfg = ESAModelConfig(vocab_size=256, block=512, n_layer=2, head=4, embd=64, dropout=0.0,
+                         precision="fp32", backend="thunder", training_compile=False)
+    a, b = ESAModel(cfg, device="cpu"), ESAModel(cfg, device="cpu")
+    fill_model(a, seed=7, n_layer=2)
+    fill_model(b, seed=7, n_layer=2)
+    for (n, p), (_, q) in zip(a.named_parameters(), b.named_parameters()):
+        assert torch.equal(p, q), n
+    assert a.lm_head.weight.data_ptr() == a.wte.weight.data_ptr()
+    assert abs(float(a.blocks[0].ln1.weight.detach().mean()) - 1.0) < 0.05
+    z = np.load(GOLDEN / "model_train_step.npz")
+    grads = {k[6:]: z[k].shape for k in z.files if k.startswith("grad::")}
+    assert {n: tuple(p.shape) for n, p in a.named_parameters()} == grads

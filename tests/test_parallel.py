@@ -141,6 +141,69 @@ def _nccl_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def _one_gpu_worker(rank, world, port, backend, q):
+    """Rank of a sequence-parallel scan whose ranks all share GPU 0 (the
+    kernels of different ranks never wait on one another: the only exchange is
+    the all-gather between the summary and the scan)."""
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root / "entangled-state-attention_v2_b200"))
+    import datetime
+    from esa import ops
+    from esa.parallel import sequence_parallel_scan
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(0)
+    kw = {"device_id": torch.device("cuda", 0)} if backend == "nccl" else {}
+    dist.init_process_group(backend, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), **kw)
+    try:
+        A, B, e0 = _sp_inputs()
+        T = A.shape[1]
+        cuts = [i * T // world for i in range(world + 1)]
+        sl = slice(cuts[rank], cuts[rank + 1])
+        E = sequence_parallel_scan(A[:, sl].cuda(), B[:, sl].cuda(), e0=e0.cuda())
+        torch.cuda.synchronize()
+        ops.check_device_status()
+        q.put((rank, E.cpu().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _sp_inputs():
+    g = torch.Generator().manual_seed(3)
+    nb, T, H, D = 2, 24576, 4, 64
+    A = torch.sigmoid(torch.randn(nb, T, H, D, generator=g) + 3)
+    B = torch.randn(nb, T, H, D, generator=g) * 0.5
+    e0 = torch.randn(nb, H * D, generator=g)
+    return A, B, e0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("backend,world", [("nccl", 1), ("gloo", 2), ("gloo", 3)])
+def test_sequence_parallel_scan_on_one_gpu(backend, world):
+    """esa.parallel.sequence_parallel_scan end to end (summary kernel,
+    all-gather, carry composition, resumed scan) with every rank on GPU 0:
+    NCCL at world size 1, gloo at 2 and 3 (slices of 8192 steps or more, so
+    the few-channel slices take the split summary / resume path); the joined slices against the fp64 oracle of the
+    whole sequence from the same initial state."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_one_gpu_worker, args=(r, world, port, backend, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    A, B, e0 = _sp_inputs()
+    nb, T, H, D = A.shape
+    ref = oracle.scan_fwd(A.double(), B.double(), e0.double().reshape(nb, H, D))
+    full = np.concatenate([got[r] for r in range(world)], axis=1)
+    assert np.linalg.norm(full - ref) / np.linalg.norm(ref) < 1e-5
+
+
 @pytest.mark.gpu
 def test_sequence_parallel_scan_nccl():
     n = torch.cuda.device_count()
