@@ -503,6 +503,25 @@ def secondary(dev, stream, L) -> dict:
                                              dv.data_ptr(), C, _lib.DTYPE_F16, nb, T, C, 0.8, 0.995, 1, 16,
                                              None, None, w.data_ptr(), wsb, sp))
     out["gated_bwd_f16_16x2048x768_GBps"] = 6 * N * 2 / (ms * 1e-3) / 1e9
+    # the fused layer core (gated scan + RMS readout, one kernel per
+    # direction): forward reads q, g, v and writes E, y (10 bytes an element);
+    # backward reads dy, q, g, v, E and writes dq, dg, dv (16 bytes)
+    y = torch.empty_like(Eg)
+    rstd = torch.empty(nb * T, device=dev)
+    dy = torch.randn(nb, T, C, device=dev, generator=g).half()
+    dqgv = torch.empty_like(qgv)
+    lwb = L.esa_layer_workspace_bytes(nb, T, C, _lib.DTYPE_F16, _lib.DTYPE_F16, _lib.DTYPE_F16)
+    lw = torch.empty(lwb, dtype=torch.uint8, device=dev)
+    ms = timeit(lambda: L.esa_layer_fwd(qgv.data_ptr(), 3 * C, _lib.DTYPE_F16, Eg.data_ptr(), _lib.DTYPE_F16,
+                                        y.data_ptr(), _lib.DTYPE_F16, rstd.data_ptr(), nb, T, C, 0.8, 0.995, 1e-5,
+                                        None, None, lw.data_ptr(), lwb, sp))
+    out["layer_fwd_f16_16x2048x768_GBps"] = 10 * N * 2 / (ms * 1e-3) / 1e9
+    out["layer_fwd_f16_16x2048x768_us"] = ms * 1e3
+    ms = timeit(lambda: L.esa_layer_bwd(dy.data_ptr(), _lib.DTYPE_F16, qgv.data_ptr(), 3 * C, _lib.DTYPE_F16,
+                                        Eg.data_ptr(), _lib.DTYPE_F16, rstd.data_ptr(), dqgv.data_ptr(), 3 * C, nb,
+                                        T, C, 0.8, 0.995, 1e-5, None, None, lw.data_ptr(), lwb, sp))
+    out["layer_bwd_f16_16x2048x768_GBps"] = 16 * N * 2 / (ms * 1e-3) / 1e9
+    out["layer_bwd_f16_16x2048x768_us"] = ms * 1e3
     return out
 
 

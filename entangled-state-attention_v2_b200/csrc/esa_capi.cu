@@ -156,7 +156,32 @@ ESA_EXPORT int esa_device_status(int device, int clear, unsigned int* status) {
 ESA_EXPORT size_t esa_scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int dtype, int compass) {
     const int es = dtype_size(dtype);
     if (es == 0 || nb < 0 || T < 0 || hd < 0 || compass <= 0) return 0;
-    return scan_workspace_bytes(nb, T, hd, es, compass);
+    const size_t scan = scan_workspace_bytes(nb, T, hd, es, compass);
+    const size_t tile = tile_gated_workspace_bytes(nb, T, hd, dtype);
+    return scan > tile ? scan : tile;
+}
+
+ESA_EXPORT size_t esa_layer_workspace_bytes(int64_t nb, int64_t T, int64_t C, int qgv_dtype, int e_dtype,
+                                            int y_dtype) {
+    return layer_workspace_bytes(nb, T, C, qgv_dtype, e_dtype, y_dtype);
+}
+
+ESA_EXPORT int esa_layer_fwd(const void* qgv, int64_t qgv_row_stride, int qgv_dtype, void* E, int e_dtype, void* y,
+                             int y_dtype, void* rstd, int64_t nb, int64_t T, int64_t C, double gate_min,
+                             double gate_max, double eps, const void* e0, void* e_last, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    clear_error();
+    return layer_fwd(qgv, qgv_row_stride, qgv_dtype, E, e_dtype, y, y_dtype, rstd, nb, T, C, gate_min, gate_max, eps,
+                     e0, e_last, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+ESA_EXPORT int esa_layer_bwd(const void* dy, int dy_dtype, const void* qgv, int64_t qgv_row_stride, int qgv_dtype,
+                             const void* E, int e_dtype, const void* rstd, void* dqgv, int64_t dqgv_row_stride,
+                             int64_t nb, int64_t T, int64_t C, double gate_min, double gate_max, double eps,
+                             const void* e0, void* de0, void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    return layer_bwd(dy, dy_dtype, qgv, qgv_row_stride, qgv_dtype, E, e_dtype, rstd, dqgv, dqgv_row_stride, nb, T, C,
+                     gate_min, gate_max, eps, e0, de0, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 ESA_EXPORT int esa_scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd,

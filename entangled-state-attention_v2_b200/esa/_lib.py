@@ -68,6 +68,11 @@ SIGNATURES = {
                                   _vp]),
     "esa_lightning_step": (_int, [_vp, _i64, _int, _vp, _vp, _int, _vp, _int, _i64, _i64, _f64,
                                   _f64, _f64, _vp]),
+    "esa_layer_workspace_bytes": (_sz, [_i64, _i64, _i64, _int, _int, _int]),
+    "esa_layer_fwd": (_int, [_vp, _i64, _int, _vp, _int, _vp, _int, _vp, _i64, _i64, _i64, _f64, _f64, _f64,
+                             _vp, _vp, _vp, _sz, _vp]),
+    "esa_layer_bwd": (_int, [_vp, _int, _vp, _i64, _int, _vp, _int, _vp, _vp, _i64, _i64, _i64, _i64, _f64,
+                             _f64, _f64, _vp, _vp, _vp, _sz, _vp]),
 }
 
 
@@ -116,12 +121,12 @@ def check(rc: int, what: str) -> None:
     raise RuntimeError(f"{what} failed ({rc}): {msg}")
 
 
-SCAN_PATHS = {0: "none", 1: "sequential", 2: "lookback", 3: "strip", 4: "lane"}
+SCAN_PATHS = {0: "none", 1: "sequential", 2: "lookback", 3: "strip", 4: "lane", 5: "rowtile"}
 
 
 def last_scan_path() -> str:
     """Kernel family of the last scan launch on this host thread: "sequential",
-    "lookback", "strip" or "lane" ("none" before any)."""
+    "lookback", "strip", "lane" or "rowtile" ("none" before any)."""
     return SCAN_PATHS.get(int(lib().esa_scan_last_path()), "unknown")
 
 

@@ -387,7 +387,6 @@ def layer_core(qgv: Tensor, gate_min: float, gate_max: float, eps: float, compas
     _require_cuda("esa layer core", qgv)
     qgv, nb, T, C = _core_views(qgv)
     L = _lib.lib()
-    es = qgv.element_size()
     rdt = dtype_code(qgv.dtype)
     acc = acc_dtype(scan_dtype, qgv.dtype, out_dtype)
     E = torch.empty(nb, T, C, dtype=scan_dtype, device=qgv.device)
@@ -395,17 +394,19 @@ def layer_core(qgv: Tensor, gate_min: float, gate_max: float, eps: float, compas
     rstd = torch.empty(nb * T, dtype=acc, device=qgv.device)
     if nb * T * C == 0:
         return y, E, rstd
-    base = qgv.data_ptr()
-    ws = _workspace(nb, T, C, _widest(qgv.dtype, scan_dtype), compass, qgv.device)
-    s = _stream(qgv)
-    _lib.check(L.esa_gated_scan_fwd(base + C * es, base + 2 * C * es, 3 * C, rdt, E.data_ptr(),
-                                    dtype_code(scan_dtype), nb, T, C, float(gate_min), float(gate_max),
-                                    1, int(compass), None, None, ws.data_ptr(), ws.numel(), s),
-               "esa_gated_scan_fwd")
-    _lib.check(L.esa_readout_fwd(base, 3 * C, rdt, E.data_ptr(), C, dtype_code(scan_dtype), y.data_ptr(),
-                                 C, dtype_code(out_dtype), rstd.data_ptr(), nb * T, C, float(eps), s),
-               "esa_readout_fwd")
+    ws = _layer_workspace(nb, T, C, qgv.dtype, scan_dtype, out_dtype, qgv.device)
+    _lib.check(L.esa_layer_fwd(qgv.data_ptr(), 3 * C, rdt, E.data_ptr(), dtype_code(scan_dtype), y.data_ptr(),
+                               dtype_code(out_dtype), rstd.data_ptr(), nb, T, C, float(gate_min), float(gate_max),
+                               float(eps), None, None, ws.data_ptr(), ws.numel(), _stream(qgv)), "esa_layer_fwd")
     return y, E, rstd
+
+
+def _layer_workspace(nb: int, T: int, C: int, qdt: torch.dtype, edt: torch.dtype, ydt: torch.dtype,
+                     device) -> Tensor:
+    n = _lib.lib().esa_layer_workspace_bytes(nb, T, C, dtype_code(qdt), dtype_code(edt), dtype_code(ydt))
+    if n == 0:
+        raise ValueError("invalid layer problem")
+    return torch.empty(int(n), dtype=torch.uint8, device=device)
 
 
 @layer_core.register_fake
@@ -419,30 +420,23 @@ def _(qgv, gate_min, gate_max, eps, compass, scan_dtype, out_dtype):
 @torch.library.custom_op("esa_b200::layer_core_backward", mutates_args=())
 def layer_core_backward(dy: Tensor, qgv: Tensor, E: Tensor, rstd: Tensor, gate_min: float,
                         gate_max: float, eps: float, compass: int) -> Tensor:
-    """d qgv [B,T,3C] (qgv's dtype): the readout backward writes the q third
-    and dE, the gated reverse scan the g and v thirds."""
+    """d qgv [B,T,3C] (qgv's dtype): dq from the readout backward, d gate and
+    d value from the gated reverse scan (one fused kernel where the shape and
+    dtypes allow)."""
     _require_cuda("esa layer core backward", dy, qgv, E, rstd)
     qgv, nb, T, C = _core_views(qgv)
     dy = dy.contiguous()
     E = E.contiguous()
     L = _lib.lib()
-    es = qgv.element_size()
     rdt = dtype_code(qgv.dtype)
-    edt = dtype_code(E.dtype)
     dqgv = torch.empty_like(qgv)
     if nb * T * C == 0:
         return dqgv.zero_()
-    dE = torch.empty_like(E)
-    base, dbase = qgv.data_ptr(), dqgv.data_ptr()
-    s = _stream(qgv)
-    _lib.check(L.esa_readout_bwd(dy.data_ptr(), C, dtype_code(dy.dtype), base, 3 * C, rdt, E.data_ptr(), C,
-                                 edt, rstd.data_ptr(), dbase, 3 * C, rdt, dE.data_ptr(), C, edt, nb * T, C,
-                                 float(eps), s), "esa_readout_bwd")
-    ws = _workspace(nb, T, C, _widest(qgv.dtype, E.dtype), compass, qgv.device)
-    _lib.check(L.esa_gated_scan_bwd(base + C * es, base + 2 * C * es, 3 * C, rdt, E.data_ptr(), dE.data_ptr(),
-                                    edt, dbase + C * es, dbase + 2 * C * es, 3 * C, rdt, nb, T, C,
-                                    float(gate_min), float(gate_max), 1, int(compass), None, None,
-                                    ws.data_ptr(), ws.numel(), s), "esa_gated_scan_bwd")
+    ws = _layer_workspace(nb, T, C, qgv.dtype, E.dtype, dy.dtype, qgv.device)
+    _lib.check(L.esa_layer_bwd(dy.data_ptr(), dtype_code(dy.dtype), qgv.data_ptr(), 3 * C, rdt, E.data_ptr(),
+                               dtype_code(E.dtype), rstd.data_ptr(), dqgv.data_ptr(), 3 * C, nb, T, C,
+                               float(gate_min), float(gate_max), float(eps), None, None, ws.data_ptr(), ws.numel(),
+                               _stream(qgv)), "esa_layer_bwd")
     return dqgv
 
 

@@ -153,6 +153,21 @@ def readout(q, E, eps=1e-5):
     return z
 
 
+def readout_bwd(q, E, rstd, dy):
+    """fp64 gradient of the readout y = sigmoid(q) * E * r, r = rsqrt(mean_C(E^2)
+    + eps) given per row as `rstd` (thunder.py:304-311, differentiated through
+    r as autograd does): dq = dy n s (1 - s), dE = r (dy s - n mean_C(dy s n))
+    with s = sigmoid(q), n = E r.  Returns (dq, dE)."""
+    q, E, dy = _f64(q), _f64(E), _f64(dy)
+    r = _f64(rstd).reshape(E.shape[:-1] + (1,))
+    s = 1.0 / (1.0 + np.exp(-q))
+    n = E * r
+    t1 = dy * s
+    dq = t1 * n * (1.0 - s)
+    dE = r * (t1 - n * np.mean(t1 * n, axis=-1, keepdims=True))
+    return dq, dE
+
+
 def scan_fwd_f32_scalar(A: np.ndarray, B: np.ndarray) -> np.ndarray:
     """Single-threaded fp32 scalar scan (a timed CPU baseline)."""
     A = np.ascontiguousarray(A, dtype=np.float32)

@@ -27,7 +27,8 @@ def test_header_declares_the_abi():
         "esa_scan_host_staging_bytes", "esa_scan_fwd_host", "esa_scan_fwd_resume",
         "esa_wait_selftest", "esa_readout_fwd", "esa_readout_bwd", "esa_layer_norm_fwd",
         "esa_layer_norm_workspace_bytes", "esa_layer_norm_bwd", "esa_add_layer_norm_fwd",
-        "esa_add_layer_norm_bwd", "esa_cross_entropy_fwd", "esa_cross_entropy_bwd"}
+        "esa_add_layer_norm_bwd", "esa_cross_entropy_fwd", "esa_cross_entropy_bwd",
+        "esa_layer_workspace_bytes", "esa_layer_fwd", "esa_layer_bwd"}
 
 
 def test_library_loads_and_exports_every_declared_symbol():
@@ -249,3 +250,33 @@ def test_seeded_weights_cover_the_model_fixtures():
     z = np.load(GOLDEN / "model_train_step.npz")
     grads = {k[6:]: z[k].shape for k in z.files if k.startswith("grad::")}
     assert {n: tuple(p.shape) for n, p in a.named_parameters()} == grads
+
+
+def test_layer_core_entry_points_need_no_gpu_for_sizes_and_errors():
+    """esa_layer_workspace_bytes is host arithmetic (the fused kernel's
+    look-back descriptors, or the two-kernel form's scan workspace plus its dE
+    buffer); esa_layer_fwd / esa_layer_bwd reject bad arguments before any
+    device work."""
+    from esa import _lib
+    L = _lib.lib()
+    F16, F32 = _lib.DTYPE_F16, _lib.DTYPE_F32
+    fused = L.esa_layer_workspace_bytes(16, 2048, 768, F16, F16, F16)
+    # tiles of 8 steps x 768 channels (the backward's): three fp32 planes
+    ntiles = 16 * 2048 // 8
+    assert fused >= 3 * ntiles * 768 * 4
+    assert fused < 4 * ntiles * 768 * 4
+    two_kernel = L.esa_layer_workspace_bytes(2, 300, 96, F32, F32, F32)  # C not a multiple of 64
+    assert two_kernel >= 2 * 300 * 96 * 4                                # holds dE
+    assert L.esa_layer_workspace_bytes(2, 300, 96, 9, F32, F32) == 0
+    assert L.esa_layer_workspace_bytes(2, 300, 0, F32, F32, F32) == 0
+    rc = L.esa_layer_fwd(None, 100, F16, None, F16, None, F16, None, 2, 8, 64, 0.8, 0.995, 1e-5,
+                         None, None, None, 0, None)
+    assert rc == -1 and "row stride" in _lib.last_error()
+    rc = L.esa_layer_fwd(None, 192, F16, None, F16, None, F16, None, 2, 8, 64, 0.8, 0.995, 1e-5,
+                         None, None, None, 0, None)
+    assert rc == -1 and "null" in _lib.last_error()
+    rc = L.esa_layer_bwd(None, F16, None, 192, 7, None, F16, None, None, 192, 2, 8, 64, 0.8, 0.995,
+                         1e-5, None, None, None, 0, None)
+    assert rc == -2
+    assert L.esa_layer_fwd(None, 192, F16, None, F16, None, F16, None, 0, 8, 64, 0.8, 0.995, 1e-5,
+                           None, None, None, 0, None) == 0  # empty problem
