@@ -31,22 +31,12 @@ namespace {
 
 constexpr int kMaxSlots = 8;
 
-int env_int(const char* name, int dflt, int lo, int hi) {
-    const char* v = getenv(name);
-    const int x = v ? atoi(v) : 0;
-    return (x >= lo && x <= hi) ? x : dflt;
-}
-// staging slots and chunk size per array (tuning overrides ESA_HOST_SLOTS,
-// ESA_HOST_CHUNK_MB, read once)
-int slots() {
-    static const int s = env_int("ESA_HOST_SLOTS", 3, 2, kMaxSlots);
-    return s;
-}
+// staging slots per array (more than 3 gained nothing)
+int slots() { return 3; }
 int64_t chunk_bytes() {
     // 32 MB: measured 70 GB/s end to end on [32,4096,16,64] fp16 against 65 at
     // 8 MB (per-copy overheads); more slots than 3 gained nothing
-    static const int64_t b = (int64_t)env_int("ESA_HOST_CHUNK_MB", 32, 1, 256) << 20;
-    return b;
+    return (int64_t)32 << 20;
 }
 
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }

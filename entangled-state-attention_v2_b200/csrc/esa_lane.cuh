@@ -27,6 +27,8 @@
 // two are interchangeable behind strip_scan_launch.
 #pragma once
 
+#include <atomic>
+
 #include "esa_strip.cuh"
 
 namespace esa {
@@ -287,10 +289,13 @@ int lane_launch_typed(const ScanCall& call, int nstage, int grid) {
 template <Kind K, typename Tin, typename Te, int NW, bool SUMM>
 int lane_occupancy(int dev, int nstage) {
     using Cfg = LaneCfg<K, Tin, Te, NW>;
-    static int cache[16][17];  // [device][nstage]: 0 unknown, -1 none, else occupancy
+    // [device][nstage]: 0 unknown, -1 none, else occupancy (atomic: see
+    // strip_occupancy)
+    static std::atomic<int> cache[16][17];
     if (dev < 0 || dev >= 16 || nstage < 1 || nstage > 16) return 0;
-    int& slot = cache[dev][nstage];
-    if (slot != 0) return slot < 0 ? 0 : slot;
+    std::atomic<int>& slot = cache[dev][nstage];
+    const int known = slot.load(std::memory_order_relaxed);
+    if (known != 0) return known < 0 ? 0 : known;
     const size_t smem = Cfg::smem_bytes(nstage);
     int per_sm = 0;
     if (smem <= 232448 &&
@@ -299,17 +304,14 @@ int lane_occupancy(int dev, int nstage) {
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lane_scan_kernel<K, Tin, Te, NW, SUMM>, Cfg::NT,
                                                       smem) == cudaSuccess &&
         per_sm > 0) {
-        slot = per_sm;
+        slot.store(per_sm, std::memory_order_relaxed);
     } else {
-        slot = -1;
+        slot.store(-1, std::memory_order_relaxed);
         per_sm = 0;
     }
     return per_sm;
 }
 
-// Tuning overrides (0 = automatic): ESA_LANE_NW (1 or 2 consumer warps per
-// CTA) and ESA_LANE_STAGES (2..16).
-//
 // Picks the consumer warps per CTA and the ring depth, or declines
 // (*taken = false) when the lanes cannot fill the GPU: fewer than
 // `min_warps_per_sm` consumer warps per SM.  The ring holds at least
@@ -322,24 +324,21 @@ int lane_launch_kind(const ScanCall& call, bool* taken, double min_warps_per_sm)
     const int sms = device_sm_count(dev);
     const int64_t nb = call.a.nb * (call.npiece > 1 ? call.npiece : 1), hd = call.a.hd;
     if (call.a.T < 16) return ESA_OK;
-    static const int force_nw = strip_env("ESA_LANE_NW");
-    static const int force_ns = strip_env("ESA_LANE_STAGES");
     using C1 = LaneCfg<K, Tin, Te, 1>;
     const int64_t warps = nb * ((hd + C1::WS - 1) / C1::WS);
     if ((double)warps < min_warps_per_sm * sms) return ESA_OK;
     // two consumer warps (256-byte rows) when every SM still gets a CTA
     // (fp16 forward, us: [32,4096,16,64] 132.8 vs 134.3 with one warp;
     // [74,2048,16,64] 158.2 vs 180.0; [128,1024,16,64] 138.0 vs 154.1)
-    // an override other than 1 or 2 falls back to the automatic choice
-    int nw = (force_nw == 1 || force_nw == 2) ? force_nw : 1;
-    if (force_nw != 1 && force_nw != 2) {
+    int nw = 1;
+    {
         using C2 = LaneCfg<K, Tin, Te, 2>;
         const int64_t ctas2 = nb * ((hd + C2::WS - 1) / C2::WS);
         nw = ctas2 >= (int64_t)sms ? 2 : 1;
     }
     const int stage = nw == 2 ? LaneCfg<K, Tin, Te, 2>::stage_bytes() : C1::stage_bytes();
-    int ns = force_ns;
-    if (!ns) {
+    int ns = 0;
+    {
         // about 16 KB of tiles in flight per consumer warp (the
         // [32,4096,16,64] fp16 forward with one consumer warp: 134.9 us at
         // three 8 KB stages against 150.7 at two and 147.5 / 161.6 / 217.2 at

@@ -39,8 +39,9 @@ int lane_fwd_gated(const ScanCall& c, bool* taken, double min_warps);
 int lane_rev_gated(const ScanCall& c, bool* taken, double min_warps);
 
 namespace {
-// ESA_SCAN_PATH: "lane" (lane-serial whenever it applies), "strip" (never
-// lane-serial), "lookback" (see run()); unset: automatic.
+// ESA_SCAN_PATH=lane runs every scan kind on the lane-serial kernel where it
+// applies (the test suite's second pass over the scan tests); unset or any
+// other value: the automatic choice.
 std::string scan_path_env() {
     const char* v = getenv("ESA_SCAN_PATH");
     return v != nullptr ? std::string(v) : std::string();
@@ -58,7 +59,6 @@ constexpr double kLaneMinWarps = 2.0;
 int lane_scan_launch(const ScanCall& c, bool* taken) {
     static const std::string path = scan_path_env();
     *taken = false;
-    if (path == "strip") return ESA_OK;
     const bool forced = path == "lane";
     const double mw = forced ? 0.0 : kLaneMinWarps;
     const bool fwd16 = (c.kind == Kind::FwdPlain || c.kind == Kind::FwdSummary) && dtype_size(c.te) == 2;
@@ -296,12 +296,6 @@ int run(ScanCall& c) {
     bool done = false;
     if (int rc = run_split(c, &done)) return rc;
     if (done) return ESA_OK;
-    // tuning override: ESA_SCAN_PATH=lookback skips the strip scan
-    static const bool force_lookback = [] {
-        const char* v = getenv("ESA_SCAN_PATH");
-        return v != nullptr && std::string(v) == "lookback";
-    }();
-    if (force_lookback && c.kind != Kind::FwdSummary) return lookback_scan_launch(c);
     bool taken = false;
     const int rc = strip_scan_launch(c, &taken);
     if (rc != ESA_OK || taken) return rc;
@@ -316,12 +310,6 @@ struct SplitPlan {
     int64_t npiece = 1, plen = 0;
 };
 
-int split_env(const char* name, int dflt) {
-    const char* v = getenv(name);
-    const int x = v ? atoi(v) : 0;
-    return x > 0 ? x : dflt;
-}
-
 // Pieces per batch row for an [nb, T, hd] problem whose widest element has
 // `wide_es` bytes: split when 128-channel-wide strips (16 lanes) number fewer
 // than one per SM of a B200 and the time axis is long (>= 8192 steps; shorter
@@ -331,10 +319,7 @@ int split_env(const char* name, int dflt) {
 // multiple of 64 steps (every strip tile length divides 64).
 
 SplitPlan split_plan(int64_t nb, int64_t T, int64_t hd, int wide_es) {
-    // tuning overrides, read once: ESA_SPLIT_MIN_T, ESA_SPLIT_TARGET, ESA_SPLIT_MIN_PIECE
-    static const int min_t = split_env("ESA_SPLIT_MIN_T", 8192);
-    static const int target = split_env("ESA_SPLIT_TARGET", 2400);
-    static const int min_piece = split_env("ESA_SPLIT_MIN_PIECE", 1024);
+    constexpr int min_t = 8192, target = 2400, min_piece = 1024;
     SplitPlan p;
     if (wide_es <= 0 || T < min_t) return p;
     const int64_t ws16 = 16 * (16 / wide_es);

@@ -38,6 +38,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -452,13 +453,6 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
         mbar_wait_bounded(&bars[u % nstage], (unsigned)((u / nstage) & 1), ka.status);
 }
 
-// Tuning overrides read once from the environment (0 = automatic):
-// ESA_STRIP_LPR (4/8/16/32 lanes per row) and ESA_STRIP_STAGES (2..8).
-inline int strip_env(const char* name) {
-    const char* v = getenv(name);
-    return v ? atoi(v) : 0;
-}
-
 // Build a 3-D tensor map [nb][T][hd] (row stride rs elements) with box
 // [1][LT][WS] for dtype code `dtype`; L2 promotion of `promo_bytes` (256,
 // 128, 64 or 0 = none).
@@ -510,10 +504,14 @@ int strip_launch_typed(const ScanCall& call, int nstage, int grid) {
 template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM>
 int strip_occupancy(int dev, int nstage) {
     using Cfg = StripCfg<K, Tin, Te, LPR, SR>;
-    static int cache[16][9];  // [device][nstage]: 0 unknown, -1 none, else occupancy
+    // [device][nstage]: 0 unknown, -1 none, else occupancy; atomic so that
+    // concurrent first calls from several host threads are well defined (they
+    // compute the same value)
+    static std::atomic<int> cache[16][9];
     if (dev < 0 || dev >= 16 || nstage < 1 || nstage > 8) return 0;
-    int& slot = cache[dev][nstage];
-    if (slot != 0) return slot < 0 ? 0 : slot;
+    std::atomic<int>& slot = cache[dev][nstage];
+    const int known = slot.load(std::memory_order_relaxed);
+    if (known != 0) return known < 0 ? 0 : known;
     const size_t smem = Cfg::smem_bytes(nstage);
     int per_sm = 0;
     if (smem <= 232448 &&
@@ -522,9 +520,9 @@ int strip_occupancy(int dev, int nstage) {
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM>,
                                                       Cfg::NT, smem) == cudaSuccess &&
         per_sm > 0) {
-        slot = per_sm;
+        slot.store(per_sm, std::memory_order_relaxed);
     } else {
-        slot = -1;
+        slot.store(-1, std::memory_order_relaxed);
         per_sm = 0;
     }
     return per_sm;
@@ -547,8 +545,6 @@ int strip_launch_kind(const ScanCall& call, bool* taken) {
     const int64_t T = call.a.T, nb = call.a.nb * (call.npiece > 1 ? call.npiece : 1), hd = call.a.hd;
     using P = Policy<K, Tin, Te>;
     if (T < 16) return ESA_OK;
-    static const int force_lpr = strip_env("ESA_STRIP_LPR");
-    static const int force_ns = strip_env("ESA_STRIP_STAGES");
     auto strips = [&](int lpr) { return nb * ((hd + lpr * P::VEC - 1) / (lpr * P::VEC)); };
     auto occ = [&](int lpr, int ns) -> int {
         switch (lpr) {
@@ -561,7 +557,6 @@ int strip_launch_kind(const ScanCall& call, bool* taken) {
     int pick_lpr = 0, pick_ns = 0, pick_occ = 0;
     double best = 0.0;
     for (int lpr : {32, 16, 8, 4}) {
-        if (force_lpr && lpr != force_lpr) continue;
         const int64_t n = strips(lpr);
         if (n < (sms * 3) / 4) continue;  // too few strips to fill the GPU
         // two stages (measured: never slower than 3-6, and 8 % faster on the
@@ -570,12 +565,11 @@ int strip_launch_kind(const ScanCall& call, bool* taken) {
         // three when they keep the occupancy of two (237.8 vs 243.9 us on
         // [32,4096,16,64] fp16: its stages hold 32 steps, not 64).
         int ns = 0, o = 0;
-        if (!force_ns && K == Kind::RevPlain && sizeof(Te) == 2 && occ(lpr, 3) >= occ(lpr, 2) && occ(lpr, 3) > 0) {
+        if (K == Kind::RevPlain && sizeof(Te) == 2 && occ(lpr, 3) >= occ(lpr, 2) && occ(lpr, 3) > 0) {
             ns = 3;
             o = occ(lpr, 3);
         }
         for (int s = 2; s <= 6 && ns == 0; ++s) {
-            if (force_ns && s != force_ns) continue;
             const int os = occ(lpr, s);
             if (os > o) {
                 o = os;

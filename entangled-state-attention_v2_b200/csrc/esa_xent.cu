@@ -171,7 +171,10 @@ __global__ void __launch_bounds__(kXentThreads) xent_bwd_kernel(const XentArgs a
         T* dr = reinterpret_cast<T*>(a.dz) + row * a.dld;
         const int64_t t = a.t[row];
         const bool ignored = t == a.ignore;
-        const float g = ignored ? 0.f : a.g[row];
+        // a target outside [0, V) that is not ignored gives a NaN gradient
+        // row, as its loss is NaN (never a silently plausible gradient)
+        const bool bad = !ignored && (t < 0 || t >= a.V);
+        const float g = ignored ? 0.f : (bad ? __int_as_float(0x7fffffff) : a.g[row]);
         const float l = a.lse[row];
         if constexpr (VECT) {
             const int64_t nvec = a.V / PER;

@@ -1,3 +1,9 @@
+# Copyright 2026 Zameer Hussain and Akhtar Hussain
+# Licensed under the Apache License, Version 2.0.
+# Portions of this file reproduce the public interface of esa/constants.py of
+# Entangled-State-Attention v2.1.1 (signatures, dataclasses, validation and
+# error messages), under that licence.
+
 """ESA algorithm constants (values of esa/constants.py:6-10 in the reference)."""
 
 from __future__ import annotations

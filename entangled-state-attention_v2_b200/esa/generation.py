@@ -1,3 +1,9 @@
+# Copyright 2026 Zameer Hussain and Akhtar Hussain
+# Licensed under the Apache License, Version 2.0.
+# Portions of this file reproduce the public interface of esa/generation.py of
+# Entangled-State-Attention v2.1.1 (signatures, dataclasses, validation and
+# error messages), under that licence.
+
 """Prefill and ESA-Lightning decode on the B200 kernels.
 
 Public surface of the reference's esa/generation.py (:15-560): GenerationStats,

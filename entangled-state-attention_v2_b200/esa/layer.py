@@ -1,3 +1,9 @@
+# Copyright 2026 Zameer Hussain and Akhtar Hussain
+# Licensed under the Apache License, Version 2.0.
+# Portions of this file reproduce the public interface of esa/layer.py of
+# Entangled-State-Attention v2.1.1 (signatures, dataclasses, validation and
+# error messages), under that licence.
+
 """Public ESA layer -- the drop-in boundary.
 
 Same constructor, attributes, validation messages and methods as the

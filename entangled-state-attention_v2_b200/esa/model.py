@@ -1,3 +1,9 @@
+# Copyright 2026 Zameer Hussain and Akhtar Hussain
+# Licensed under the Apache License, Version 2.0.
+# Portions of this file reproduce the public interface of esa/model.py of
+# Entangled-State-Attention v2.1.1 (signatures, dataclasses, validation and
+# error messages), under that licence.
+
 """ESAModel: the causal LM driver of the ESA layers (reference esa/model.py).
 
 Same configuration dataclass, module tree, parameter names (state_dict keys),

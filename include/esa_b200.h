@@ -141,7 +141,8 @@ int esa_cross_entropy_fwd(const void *logits, int64_t row_stride, int dtype, con
  * (exp(logits[i, j] - lse[i]) - [j == targets[i]]), zero on ignored rows,
  * written in the logits' dtype (row stride `dlogits_row_stride`).  grad_rows:
  * fp32 [rows], the gradient of the loss w.r.t. each row's loss[i] (for a mean
- * over n rows: the upstream gradient / n). */
+ * over n rows: the upstream gradient / n).  A row whose target is outside
+ * [0, V) and not ignore_index gets NaN gradients (its loss is NaN). */
 int esa_cross_entropy_bwd(const void *logits, int64_t row_stride, int dtype, const int64_t *targets,
                           int64_t ignore_index, const float *lse, const float *grad_rows, void *dlogits,
                           int64_t dlogits_row_stride, int64_t rows, int64_t V, void *stream);

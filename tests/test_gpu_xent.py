@@ -62,6 +62,19 @@ def test_cross_entropy_all_ignored_is_nan_like_torch():
     assert torch.isnan(F.cross_entropy(z, t, ignore_index=-1))
 
 
+def test_cross_entropy_out_of_range_target_poisons_its_row():
+    """A target outside [0, V) that is not ignore_index: NaN loss, and NaN
+    gradients on that row only (the other rows keep theirs)."""
+    from esa import ops
+    z = torch.randn(6, 64, device="cuda", requires_grad=True)
+    t = torch.tensor([3, 70, 5, -1, 0, 63], dtype=torch.int64, device="cuda")
+    loss = ops.cross_entropy(z, t, ignore_index=-1)
+    assert torch.isnan(loss)
+    loss.backward()
+    assert torch.isnan(z.grad[1]).all()
+    assert torch.isfinite(z.grad[[0, 2, 3, 4, 5]]).all()
+
+
 def test_model_loss_with_fused_cross_entropy():
     """ESAModel (fp32) loss and gradients with the fused loss against the same
     model on F.cross_entropy."""

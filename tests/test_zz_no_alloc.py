@@ -35,19 +35,19 @@ def _inputs(shape, dtype, seed):
     return A, B
 
 
-def _noalloc(L, A, B, compass=16, e_last=None):
+def _noalloc(L, A, B, compass=16, e_last=None, e0=None):
     from esa import _lib, ops
     nb, T, H, D = A.shape
     E = torch.empty_like(A)
     rc = L.esa_scan_fwd_noalloc(A.data_ptr(), B.data_ptr(), E.data_ptr(), nb, T, H * D,
-                                ops.dtype_code(A.dtype), compass, None,
+                                ops.dtype_code(A.dtype), compass, None if e0 is None else e0.data_ptr(),
                                 None if e_last is None else e_last.data_ptr(),
                                 torch.cuda.current_stream().cuda_stream)
     assert rc == 0, _lib.last_error()
     return E
 
 
-def _with_workspace(L, A, B, compass=16):
+def _with_workspace(L, A, B, compass=16, e0=None):
     from esa import _lib, ops
     nb, T, H, D = A.shape
     E = torch.empty_like(A)
@@ -55,7 +55,8 @@ def _with_workspace(L, A, B, compass=16):
     n = L.esa_scan_workspace_bytes(nb, T, H * D, code, compass)
     ws = torch.empty(max(n, 256), dtype=torch.uint8, device="cuda")
     rc = L.esa_scan_fwd(A.data_ptr(), B.data_ptr(), E.data_ptr(), nb, T, H * D, code, compass,
-                        None, None, ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream)
+                        None if e0 is None else e0.data_ptr(), None, ws.data_ptr(), ws.numel(),
+                        torch.cuda.current_stream().cuda_stream)
     assert rc == 0, _lib.last_error()
     return E
 
@@ -73,6 +74,25 @@ def test_noalloc_matches_workspace_entry_point_two_calls(dtype):
         torch.cuda.synchronize()
         assert _rel(got, ref) < TOL[dtype], (shape, _rel(got, ref))
         assert _rel(e_last, ref[:, -1].reshape(shape[0], -1)) < TOL[dtype]
+    assert _lib.device_status(torch.cuda.current_device()) == 0
+
+
+def test_noalloc_with_initial_state_and_unaligned_rows():
+    """Prefill with a state (a non-null fp32 e0) and rows whose byte length is
+    not a multiple of 16 (fp16 with hd = 6, which takes the one-thread-per-
+    channel kernel): the same results as esa_scan_fwd, again two calls in a
+    row."""
+    from esa import _lib
+    L = _lib.lib()
+    cases = (((3, 500, 2, 64), torch.float32, True), ((2, 300, 2, 3), torch.float16, False))
+    for shape, dtype, with_e0 in cases:
+        A, B = _inputs(shape, dtype, 7)
+        nb, _, H, D = shape
+        e0 = torch.randn(nb, H * D, device="cuda") if with_e0 else None
+        got = _noalloc(L, A, B, 16, None, e0)
+        ref = _with_workspace(L, A, B, 16, e0)
+        torch.cuda.synchronize()
+        assert _rel(got, ref) < TOL[dtype], (shape, _rel(got, ref))
     assert _lib.device_status(torch.cuda.current_device()) == 0
 
 
