@@ -503,8 +503,9 @@ def secondary(dev, stream, L) -> dict:
                                              dv.data_ptr(), C, _lib.DTYPE_F16, nb, T, C, 0.8, 0.995, 1, 16,
                                              None, None, w.data_ptr(), wsb, sp))
     out["gated_bwd_f16_16x2048x768_GBps"] = 6 * N * 2 / (ms * 1e-3) / 1e9
-    # the fused layer core (gated scan + RMS readout, one kernel per
-    # direction): forward reads q, g, v and writes E, y (10 bytes an element);
+    # the layer core (esa_layer_fwd: gated scan, then RMS readout; backward:
+    # readout backward, then reverse gated scan), against the bytes a layer
+    # must move: forward reads q, g, v and writes E, y (10 bytes an element);
     # backward reads dy, q, g, v, E and writes dq, dg, dv (16 bytes)
     y = torch.empty_like(Eg)
     rstd = torch.empty(nb * T, device=dev)

@@ -156,9 +156,7 @@ ESA_EXPORT int esa_device_status(int device, int clear, unsigned int* status) {
 ESA_EXPORT size_t esa_scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int dtype, int compass) {
     const int es = dtype_size(dtype);
     if (es == 0 || nb < 0 || T < 0 || hd < 0 || compass <= 0) return 0;
-    const size_t scan = scan_workspace_bytes(nb, T, hd, es, compass);
-    const size_t tile = tile_gated_workspace_bytes(nb, T, hd, dtype);
-    return scan > tile ? scan : tile;
+    return scan_workspace_bytes(nb, T, hd, es, compass);
 }
 
 ESA_EXPORT size_t esa_layer_workspace_bytes(int64_t nb, int64_t T, int64_t C, int qgv_dtype, int e_dtype,

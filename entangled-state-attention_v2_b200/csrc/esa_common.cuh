@@ -143,6 +143,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
     return ok != 0;
 }
 
+// Non-blocking test of an mbarrier phase (no suspension).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, unsigned parity) {
+    uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+    return ok != 0;
+}
+
 // Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
 // global to this CTA's shared memory, completing on `bar`.  L2 evict-first:
 // every input byte is read exactly once.
@@ -173,18 +185,34 @@ __device__ __forceinline__ float sigmoid_(float x) { return sigmoidf_(x); }
 __device__ __forceinline__ float tanh_(float x) { return tanhf(x); }
 __device__ __forceinline__ double tanh_(double x) { return tanh(x); }
 
-// Gate nonlinearity of 16-bit logits feeding a 16-bit scan: CUDA's fast
-// intrinsics __expf and __fdividef for the sigmoid and the hardware tanh
-// approximation (PTX tanh.approx.f32, relative error below 2^-10.98).  Their
-// errors sit at the half-precision rounding (2^-11 relative) that the logits
-// carry in and that A, B and E get on the way out; the exact forms above cost
-// the fused gated scans a third of their speed (the [16,2048,768] fp16
-// forward: 115.7 vs 75.4 us).  Wider logits or scans keep the exact forms.
-__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+// Gate nonlinearity of 16-bit logits feeding a 16-bit scan, on the hardware
+// approximations of PTX: sigmoid(x) = 1 / (1 + 2^(-x log2 e)) with
+// ex2.approx.ftz.f32 and rcp.approx.ftz.f32 (relative errors near 2^-22), and
+// tanh.approx.f32 (relative error below 2^-10.98).  Their errors sit at or
+// below the half-precision rounding (2^-11 relative) that the logits carry in
+// and that A, B and E get on the way out; the exact forms above cost the
+// fused gated scans a third of their speed (the [16,2048,768] fp16 forward:
+// 115.7 vs 75.4 us).  Wider logits or scans keep the exact forms.
+__device__ __forceinline__ float sigmoid_fast(float x) {
+    float e, r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * -1.4426950408889634f));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.0f + e));
+    return r;
+}
 __device__ __forceinline__ float tanh_fast(float x) {
     float y;
     asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+// The forward gate A = lo + span sigmoid(x) of 16-bit scans, from
+// sigmoid(x) = (1 + tanh(x / 2)) / 2: one tanh.approx instead of ex2 + rcp.
+// Its error (under 2^-11 of span / 2) moves about 2 % of the fp16-rounded A
+// by one unit in the last place; the scan output's relative error grows from
+// 2.1e-4 (its own rounding) to 3.4e-4 on [4, 2048, 256] random logits.  The
+// reverse scans keep sigmoid_fast, whose derivative s (1 - s) needs the
+// relative accuracy tanh.approx lacks near saturation.
+__device__ __forceinline__ float gate_a_fast(float x, float lo_half_span, float half_span) {
+    return fmaf(half_span, tanh_fast(0.5f * x), lo_half_span);
 }
 template <bool FAST, typename A>
 __device__ __forceinline__ A gate_sigmoid(A x) {

@@ -130,9 +130,8 @@ int cross_entropy_fwd(const void* logits, int64_t ld, int dtype, const int64_t* 
 int cross_entropy_bwd(const void* logits, int64_t ld, int dtype, const int64_t* targets, int64_t ignore_index,
                       const float* lse, const float* grad_rows, void* dlogits, int64_t dld, int64_t rows, int64_t V,
                       cudaStream_t s);
-// Fused ESA layer core (esa_tile_api.cu): gated scan + RMS readout, one
-// row-tile kernel per direction where the shape and dtypes allow, else the
-// gated scan and readout kernels in turn.
+// ESA layer core (esa_layer.cu): the gated scan and the RMS readout kernels
+// in turn (forward), the readout backward and the reverse gated scan.
 size_t layer_workspace_bytes(int64_t nb, int64_t T, int64_t C, int qdt, int edt, int ydt);
 int layer_fwd(const void* qgv, int64_t qrs, int qdt, void* E, int edt, void* y, int ydt, void* rstd, int64_t nb,
               int64_t T, int64_t C, double gmin, double gmax, double eps, const void* e0, void* e_last, void* ws,
@@ -140,13 +139,6 @@ int layer_fwd(const void* qgv, int64_t qrs, int qdt, void* E, int edt, void* y, 
 int layer_bwd(const void* dy, int dydt, const void* qgv, int64_t qrs, int qdt, const void* E, int edt,
               const void* rstd, void* dqgv, int64_t dqrs, int64_t nb, int64_t T, int64_t C, double gmin, double gmax,
               double eps, const void* e0, void* de0, void* ws, size_t ws_bytes, cudaStream_t s);
-// The bare gated scans on the row-tile kernel; *taken = false leaves the
-// call to the strip / lane / look-back kernels.
-int tile_gated_fwd(const ScanCall& c, bool* taken);
-int tile_gated_bwd(const ScanCall& c, bool* taken);
-// Workspace the row-tile gated scans need for [nb, T, hd] whose widest
-// element type is `dtype` (0 when no row-tile plan applies).
-size_t tile_gated_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int dtype);
 int lightning_step(const void* qgv, int64_t qrs, int qdt, const void* state, void* new_state,
                    int sdt, void* z, int zdt, int64_t nb, int64_t C, double gmin, double gmax,
                    double eps, cudaStream_t s);

@@ -576,11 +576,6 @@ int gated_scan_fwd(const void* g, const void* v, int64_t rrs, int raw_dtype, voi
     c.ws_bytes = ws_bytes;
     c.stream = s;
     c.bulk_ok = rows_aligned(g, rrs, hd, ei) && rows_aligned(v, rrs, hd, ei) && rows_aligned(E, hd, hd, ee);
-    if (nb * T * hd > 0) {
-        bool taken = false;
-        if (int rc = tile_gated_fwd(c, &taken)) return rc;
-        if (taken) return ESA_OK;
-    }
     return run(c);
 }
 
@@ -621,11 +616,6 @@ int gated_scan_bwd(const void* g, const void* v, int64_t rrs, int raw_dtype, con
     c.stream = s;
     c.bulk_ok = rows_aligned(g, rrs, hd, ei) && rows_aligned(v, rrs, hd, ei) && rows_aligned(E, hd, hd, ee) &&
                 rows_aligned(dE, hd, hd, ee) && rows_aligned(dg, drs, hd, ei) && rows_aligned(dv, drs, hd, ei);
-    if (nb * T * hd > 0) {
-        bool taken = false;
-        if (int rc = tile_gated_bwd(c, &taken)) return rc;
-        if (taken) return ESA_OK;
-    }
     return run(c);
 }
 

@@ -52,14 +52,16 @@ __device__ __forceinline__ double round_to(double x) {
     return static_cast<double>(Elem<T>::from_acc(static_cast<typename Elem<T>::acc>(x)));
 }
 
-template <Kind K, typename Tin, typename Te>
+// VN > 0 overrides the channels per thread vector (the narrow strip scan's
+// two-channel lanes); 0 keeps one 16-byte vector of the widest type.
+template <Kind K, typename Tin, typename Te, int VN = 0>
 struct Policy {
     static constexpr bool REV = (K == Kind::RevPlain || K == Kind::RevGated);
     static constexpr bool GATED = (K == Kind::FwdGated || K == Kind::RevGated);
     static constexpr int NIN = (K == Kind::RevGated) ? 4 : (K == Kind::RevPlain ? 3 : 2);
     using acc = typename std::conditional<(sizeof(Tin) == 8 || sizeof(Te) == 8), double, float>::type;
     static constexpr int WIDE = (sizeof(Tin) > sizeof(Te)) ? sizeof(Tin) : sizeof(Te);
-    static constexpr int VEC = 16 / WIDE;  // channels per thread vector
+    static constexpr int VEC = VN > 0 ? VN : 16 / WIDE;  // channels per thread vector
     // element size of staged array i
     static __host__ __device__ constexpr int es(int i) {
         return (K == Kind::RevGated) ? (i < 2 ? (int)sizeof(Tin) : (int)sizeof(Te))
@@ -199,6 +201,26 @@ __device__ __forceinline__ void store_global(char* p, const A (&in)[N]) {
     }
 }
 
+// Channel pairs of 16-bit data: two elements widened with one conversion,
+// and a float pair rounded to the 16-bit type and widened back (the value
+// A.to(scan_dtype) takes) with one packing conversion.
+template <typename T>
+__device__ __forceinline__ float2 pair_load(const char* p) {
+    if constexpr (std::is_same<T, __half>::value)
+        return __half22float2(*reinterpret_cast<const __half2*>(p));
+    else
+        return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+template <typename T>
+__device__ __forceinline__ float2 pair_round(float x, float y) {
+    if constexpr (std::is_same<T, __half>::value)
+        return __half22float2(__floats2half2_rn(x, y));
+    else
+        return __bfloat1622float2(__floats2bfloat162_rn(x, y));
+}
+template <typename T>
+constexpr bool is_16bit = std::is_same<T, __half>::value || std::is_same<T, __nv_bfloat16>::value;
+
 // Per-step coefficients (a, b) of step row `rows` (phase 1).  `rows[i]` points
 // at this thread's first channel in staged array i.
 template <Kind K, typename Tin, typename Te, int S, typename P = Policy<K, Tin, Te>>
@@ -209,6 +231,7 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
     using acc = typename P::acc;
     constexpr int VEC = P::VEC;
     constexpr bool FASTG = sizeof(Tin) == 2 && sizeof(Te) == 2;  // 16-bit gates (gate_sigmoid)
+    constexpr bool PAIR16 = is_16bit<Tin> && std::is_same<Tin, Te>::value && VEC % 2 == 0;
     if constexpr (K == Kind::FwdPlain || K == Kind::FwdSummary) {
         load_smem<Tin, VEC>(rows[0], a);
         load_smem<Tin, VEC>(rows[1], b);
@@ -217,6 +240,33 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
             cache.c0[s][i] = a[i];
             cache.c1[s][i] = b[i];
         }
+    } else if constexpr (K == Kind::FwdGated && PAIR16) {
+        // 16-bit logits and scan: channel pairs, B = (1 - A) tanh(v) as
+        // fma(-A, t, t) (1 - A is exact for A in [0.5, 1])
+        const float hs = 0.5f * float(prm.span), c = float(prm.gmin) + hs;
+#pragma unroll
+        for (int i = 0; i < VEC; i += 2) {
+            const float2 g = pair_load<Tin>(rows[0] + i * 2);
+            const float2 v = pair_load<Tin>(rows[1] + i * 2);
+            float A0 = gate_a_fast(g.x, c, hs), A1 = gate_a_fast(g.y, c, hs);
+            const float t0 = tanh_fast(v.x), t1 = tanh_fast(v.y);
+            float B0 = fmaf(-A0, t0, t0), B1 = fmaf(-A1, t1, t1);
+            if (prm.round_ab) {
+                const float2 ra = pair_round<Te>(A0, A1), rb = pair_round<Te>(B0, B1);
+                A0 = ra.x;
+                A1 = ra.y;
+                B0 = rb.x;
+                B1 = rb.y;
+            }
+            a[i] = A0;
+            a[i + 1] = A1;
+            b[i] = B0;
+            b[i + 1] = B1;
+            cache.c0[s][i] = A0;
+            cache.c0[s][i + 1] = A1;
+            cache.c1[s][i] = B0;
+            cache.c1[s][i + 1] = B1;
+        }
     } else if constexpr (K == Kind::FwdGated) {
         acc g[VEC], v[VEC];
         load_smem<Tin, VEC>(rows[0], g);
@@ -224,7 +274,11 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
         const acc lo = acc(prm.gmin), span = acc(prm.span);
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
-            acc A = lo + span * gate_sigmoid<FASTG>(g[i]);
+            acc A;
+            if constexpr (FASTG)
+                A = gate_a_fast(g[i], float(prm.gmin + 0.5 * prm.span), float(0.5 * prm.span));
+            else
+                A = lo + span * gate_sigmoid<FASTG>(g[i]);
             acc B = (acc(1) - A) * gate_tanh<FASTG>(v[i]);
             if (prm.round_ab) {
                 A = round_to<Te>(A);
@@ -244,6 +298,28 @@ __device__ __forceinline__ void step_coef(const char* const (&rows)[4], const KA
             b[i] = a[i] * d[i];
             cache.c0[s][i] = a[i];
             cache.c1[s][i] = d[i];
+        }
+    } else if constexpr (PAIR16) {  // RevGated, 16-bit pairs
+        const float lo = float(prm.gmin), span = float(prm.span);
+#pragma unroll
+        for (int i = 0; i < VEC; i += 2) {
+            const float2 g = pair_load<Tin>(rows[0] + i * 2);
+            const float2 d = pair_load<Te>(rows[3] + i * 2);
+            const float s0 = sigmoid_fast(g.x), s1 = sigmoid_fast(g.y);
+            float A0 = fmaf(span, s0, lo), A1 = fmaf(span, s1, lo);
+            if (prm.round_ab) {
+                const float2 ra = pair_round<Te>(A0, A1);
+                A0 = ra.x;
+                A1 = ra.y;
+            }
+            cache.c0[s][i] = s0;
+            cache.c0[s][i + 1] = s1;
+            cache.c1[s][i] = d.x;
+            cache.c1[s][i + 1] = d.y;
+            a[i] = A0;
+            a[i + 1] = A1;
+            b[i] = A0 * d.x;
+            b[i + 1] = A1 * d.y;
         }
     } else {  // RevGated
         acc g[VEC], d[VEC];
@@ -277,6 +353,7 @@ __device__ __forceinline__ void step_apply(const char* const (&rows)[4], const K
     using acc = typename P::acc;
     constexpr int VEC = P::VEC;
     constexpr bool FASTG = sizeof(Tin) == 2 && sizeof(Te) == 2;  // 16-bit gates (gate_sigmoid)
+    constexpr bool PAIR16 = is_16bit<Tin> && std::is_same<Tin, Te>::value && VEC % 2 == 0;
     if constexpr (K == Kind::FwdPlain) {
         vfma(e, cache.c0[s], e, cache.c1[s]);
         if (valid)
@@ -308,6 +385,38 @@ __device__ __forceinline__ void step_apply(const char* const (&rows)[4], const K
             if (valid) {
                 store_global<Te, VEC>(o0, ga);
                 store_global<Te, VEC>(o1, d);
+            }
+        } else if constexpr (PAIR16) {
+            acc dg[VEC], dv[VEC];
+            const float lo = float(prm.gmin), span = float(prm.span);
+#pragma unroll
+            for (int i = 0; i < VEC; i += 2) {
+                const float2 v = pair_load<Tin>(rows[1] + i * 2);
+                const float V[2] = {tanh_fast(v.x), tanh_fast(v.y)};
+                float A[2], Ar[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) A[u] = fmaf(span, cache.c0[s][i + u], lo);
+                if (prm.round_ab) {
+                    const float2 r = pair_round<Te>(A[0], A[1]);
+                    Ar[0] = r.x;
+                    Ar[1] = r.y;
+                } else {
+                    Ar[0] = A[0];
+                    Ar[1] = A[1];
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const float sg = cache.c0[s][i + u];
+                    const float g = d[i + u] + e[i + u];
+                    const float dA = g * ep[i + u];
+                    dg[i + u] = fmaf(-g, V[u], dA) * (span * sg * (1.0f - sg));
+                    dv[i + u] = g * (1.0f - A[u]) * fmaf(-V[u], V[u], 1.0f);
+                    e[i + u] = Ar[u] * g;
+                }
+            }
+            if (valid) {
+                store_global<Tin, VEC>(o0, dg);
+                store_global<Tin, VEC>(o1, dv);
             }
         } else {
             acc v[VEC], dg[VEC], dv[VEC];

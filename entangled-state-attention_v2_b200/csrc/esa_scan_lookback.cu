@@ -29,15 +29,13 @@
 // but finite result.
 #include <string>
 
-#include "esa_scan_common.cuh"
+#include "esa_lookback.cuh"
 
 namespace esa {
 
 namespace {
 
 constexpr int S = 4;  // time steps per warp per tile
-constexpr unsigned FLAG_AGG = 1, FLAG_PFX = 2;
-constexpr unsigned FULL = 0xffffffffu;
 
 struct Geometry {
     int64_t ncpr;    // channel tiles per batch row
@@ -47,14 +45,6 @@ struct Geometry {
     int nwarp;       // warps per CTA; LT = S * nwarp
 };
 
-struct Workspace {
-    unsigned* ticket;
-    unsigned* abort_flag;  // set by the first wait of this launch that runs out
-    unsigned* flags;
-    void* agg_a;
-    void* agg_b;
-    void* pref;
-};
 
 struct LbParams {
     KArgs a;
@@ -74,99 +64,6 @@ struct LbCfg {
     }
 };
 
-// Decoupled lookback, run by one warp.  Publishes the tile aggregate (ta, tb),
-// resolves the incoming carry x, publishes the inclusive prefix ta*x + tb.
-template <typename acc, int VEC>
-__device__ __forceinline__ void lookback(const Workspace& ws, unsigned* status, int64_t k,
-                                         int64_t nct, int64_t gproc, int wch, int lane,
-                                         const acc (&ta)[VEC], const acc (&tb)[VEC],
-                                         const acc (&x0)[VEC], acc (&x)[VEC], acc (&pfx)[VEC]) {
-    acc* agg_a = static_cast<acc*>(ws.agg_a);
-    acc* agg_b = static_cast<acc*>(ws.agg_b);
-    acc* pref = static_cast<acc*>(ws.pref);
-    const int64_t off = k * wch + lane * VEC;
-    if (gproc == 0) {
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) x[i] = x0[i];
-    } else {
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) {
-            agg_a[off + i] = ta[i];
-            agg_b[off + i] = tb[i];
-        }
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) st_release_gpu(ws.flags + k, FLAG_AGG);
-
-        acc ca[VEC], cb[VEC];
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) {
-            ca[i] = acc(1);
-            cb[i] = acc(0);
-        }
-        int64_t consumed = 0;
-        unsigned long long t_start = 0;
-        unsigned spins = 0;
-        while (true) {
-            const int64_t i = consumed + lane;
-            unsigned f = 0;
-            if (i < gproc) f = ld_acquire_gpu(ws.flags + (k - (i + 1) * nct));
-            const unsigned nz = __ballot_sync(FULL, f != 0);
-            const unsigned ip = __ballot_sync(FULL, f == FLAG_PFX);
-            __syncwarp();
-            const int m = (nz == FULL) ? 32 : (__ffs(~nz) - 1);
-            const unsigned mm = (m >= 32) ? FULL : ((1u << m) - 1u);
-            const unsigned pm = ip & mm;
-            const int p = pm ? (__ffs(pm) - 1) : -1;
-            const int nagg = (p >= 0) ? p : m;
-            for (int q = 0; q < nagg; ++q) {
-                const int64_t jo = (k - (consumed + q + 1) * nct) * wch + lane * VEC;
-#pragma unroll
-                for (int v = 0; v < VEC; ++v) {
-                    const acc aj = __ldcg(agg_a + jo + v);
-                    const acc bj = __ldcg(agg_b + jo + v);
-                    cb[v] = ca[v] * bj + cb[v];
-                    ca[v] = ca[v] * aj;
-                }
-            }
-            if (p >= 0) {
-                const int64_t jo = (k - (consumed + p + 1) * nct) * wch + lane * VEC;
-#pragma unroll
-                for (int v = 0; v < VEC; ++v) x[v] = ca[v] * __ldcg(pref + jo + v) + cb[v];
-                break;
-            }
-            consumed += m;
-            if (m == 0) {
-                if (spins == 0) t_start = globaltimer_ns();
-                ++spins;
-                __nanosleep(64);
-                // give up after the wait budget, or at once if another wait of
-                // this launch already gave up (no cascade of full budgets)
-                bool expired = (spins > kWaitMaxIters) ||
-                               (globaltimer_ns() - t_start > kWaitBudgetNs) ||
-                               (*(volatile unsigned*)ws.abort_flag != 0u);
-                expired = __shfl_sync(FULL, expired, 0);
-                if (expired) {
-                    if (lane == 0) {
-                        atomicOr(status, ESA_STATUS_LOOKBACK_TIMEOUT);
-                        atomicExch(ws.abort_flag, 1u);
-                    }
-#pragma unroll
-                    for (int v = 0; v < VEC; ++v) x[v] = acc(0);
-                    break;
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-        pfx[i] = ta[i] * x[i] + tb[i];
-        pref[off + i] = pfx[i];
-    }
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) st_release_gpu(ws.flags + k, FLAG_PFX);
-}
 
 struct TileCoord {
     int64_t gproc;  // processing index of the time chunk (lookback order)

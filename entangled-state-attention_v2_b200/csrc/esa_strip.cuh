@@ -46,6 +46,7 @@
 
 #include "esa_scan_common.cuh"
 
+
 namespace esa {
 
 struct StripParams {
@@ -57,9 +58,9 @@ struct StripParams {
     int nstage;
 };
 
-template <Kind K, typename Tin, typename Te, int LPR_, int SR_>
+template <Kind K, typename Tin, typename Te, int LPR_, int SR_, int VN = 0>
 struct StripCfg {
-    using P = Policy<K, Tin, Te>;
+    using P = Policy<K, Tin, Te, VN>;
     static constexpr int LPR = LPR_;
     static constexpr int SR = SR_;
     static constexpr int NW = 8;
@@ -112,6 +113,10 @@ __device__ __forceinline__ void strip_issue(const StripParams& prm, const CUtens
 template <typename A, int N, int LPR>
 __device__ __forceinline__ void lds_planar(const A* row, int cl, A (&out)[N]) {
     constexpr int PER = 16 / (int)sizeof(A);
+    if constexpr (N < PER) {  // under 16 bytes a lane: one plane
+        lds_vec<A, N>(row + cl * N, out);
+        return;
+    }
 #pragma unroll
     for (int p = 0; p < N / PER; ++p) {
         const VecN<A, PER> v = *reinterpret_cast<const VecN<A, PER>*>(row + (p * LPR + cl) * PER);
@@ -122,6 +127,10 @@ __device__ __forceinline__ void lds_planar(const A* row, int cl, A (&out)[N]) {
 template <typename A, int N, int LPR>
 __device__ __forceinline__ void sts_planar(A* row, int cl, const A (&in)[N]) {
     constexpr int PER = 16 / (int)sizeof(A);
+    if constexpr (N < PER) {
+        sts_vec<A, N>(row + cl * N, in);
+        return;
+    }
 #pragma unroll
     for (int p = 0; p < N / PER; ++p) {
         VecN<A, PER> v;
@@ -131,13 +140,13 @@ __device__ __forceinline__ void sts_planar(A* row, int cl, const A (&in)[N]) {
     }
 }
 
-template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM_>
+template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM_, int VN = 0>
 __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams prm,
                                                          const __grid_constant__ CUtensorMap m0,
                                                          const __grid_constant__ CUtensorMap m1,
                                                          const __grid_constant__ CUtensorMap m2,
                                                          const __grid_constant__ CUtensorMap m3) {
-    using Cfg = StripCfg<K, Tin, Te, LPR, SR>;
+    using Cfg = StripCfg<K, Tin, Te, LPR, SR, VN>;
     using P = typename Cfg::P;
     using acc = typename P::acc;
     constexpr int VEC = P::VEC;
@@ -282,7 +291,7 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
                         const char* rows[4];
                         rows_at(r, rows);
                         acc a[VEC], bb[VEC];
-                        step_coef<K, Tin, Te, SR>(rows, ka, a, bb, cache, s);
+                        step_coef<K, Tin, Te, SR, P>(rows, ka, a, bb, cache, s);
                         vfma(pb, a, pb, bb);
                         vmul(pa, a, pa);
                     }
@@ -385,8 +394,11 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
             char* const ob0 = ka.out[0].p + (orow0 * ka.out[0].rs + gc) * (int64_t)P::OES;
             char* const ob1 = ka.out[1].p + (orow0 * ka.out[1].rs + gc) * (int64_t)P::OES;
             const int64_t os0 = ka.out[0].rs * (int64_t)P::OES, os1 = ka.out[1].rs * (int64_t)P::OES;
-            auto phase3 = [&](auto full_tag) {
+            // MAY_T0: the tile holds step 0, whose E_{-1} is e0 (reverse kinds);
+            // every other tile reads E_{t-1} from the stage with no test on t
+            auto phase3 = [&](auto full_tag, auto t0_tag) {
                 constexpr bool FULL = decltype(full_tag)::value;
+                constexpr bool MAY_T0 = decltype(t0_tag)::value;
 #pragma unroll
                 for (int ss = 0; ss < SR; ++ss) {
                     const int s = P::REV ? (SR - 1 - ss) : ss;
@@ -395,15 +407,22 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
                     if (FULL || t < pend) {
                         const char* rows[4];
                         rows_at(r, rows);
-                        step_apply<K, Tin, Te, SR>(rows, ka, b, t, gc, valid, e, cache, s, ob0 + s * os0,
-                                                   ob1 + s * os1);
+                        step_apply<K, Tin, Te, SR, P, MAY_T0>(rows, ka, b, t, gc, valid, e, cache, s,
+                                                              ob0 + s * os0, ob1 + s * os1);
                     }
                 }
             };
-            if (rg_full)
-                phase3(std::true_type{});
-            else
-                phase3(std::false_type{});
+            if (P::REV && t0 == 0) {
+                if (rg_full)
+                    phase3(std::true_type{}, std::true_type{});
+                else
+                    phase3(std::false_type{}, std::true_type{});
+            } else {
+                if (rg_full)
+                    phase3(std::true_type{}, std::false_type{});
+                else
+                    phase3(std::false_type{}, std::false_type{});
+            }
             }
             if (last_rg) sts_planar<acc, VEC, LPR>(carry + (cur ^ 1) * WS, cl, e);
             // stage `slot` consumed, next carry visible; the whole CTA stops if
@@ -459,9 +478,9 @@ __global__ void __launch_bounds__(256, 2) strip_scan_kernel(const StripParams pr
 bool encode_strip_map(CUtensorMap* map, int dtype, const void* base, int64_t nb, int64_t T,
                       int64_t hd, int64_t rs, int ws, int lt, std::string* err, int promo_bytes = 256);
 
-template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM>
+template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM, int VN = 0>
 int strip_launch_typed(const ScanCall& call, int nstage, int grid) {
-    using Cfg = StripCfg<K, Tin, Te, LPR, SR>;
+    using Cfg = StripCfg<K, Tin, Te, LPR, SR, VN>;
     using P = typename Cfg::P;
     StripParams prm{};
     prm.a = call.a;
@@ -487,13 +506,12 @@ int strip_launch_typed(const ScanCall& call, int nstage, int grid) {
             return set_error(ESA_ERR_CUDA, "tensor map: " + err);
     }
     const size_t smem = Cfg::smem_bytes(nstage);
-    cudaError_t e = cudaFuncSetAttribute(strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    auto kern = strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM, VN>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("strip smem attribute: ") + cudaGetErrorString(e));
     if (grid > prm.nitems) grid = (int)prm.nitems;
     note_scan_path(ESA_PATH_STRIP);
-    strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM><<<grid, Cfg::NT, smem, call.stream>>>(prm, maps[0], maps[1],
-                                                                                  maps[2], maps[3]);
+    kern<<<grid, Cfg::NT, smem, call.stream>>>(prm, maps[0], maps[1], maps[2], maps[3]);
     e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(ESA_ERR_CUDA, std::string("strip scan launch: ") + cudaGetErrorString(e));
     return ESA_OK;
@@ -501,9 +519,9 @@ int strip_launch_typed(const ScanCall& call, int nstage, int grid) {
 
 // Occupancy (CTAs per SM) of a strip configuration with `nstage` stages
 // (cached per device and stage count; 0 if it cannot be resident).
-template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM>
+template <Kind K, typename Tin, typename Te, int LPR, int SR, bool SUMM, int VN = 0>
 int strip_occupancy(int dev, int nstage) {
-    using Cfg = StripCfg<K, Tin, Te, LPR, SR>;
+    using Cfg = StripCfg<K, Tin, Te, LPR, SR, VN>;
     // [device][nstage]: 0 unknown, -1 none, else occupancy; atomic so that
     // concurrent first calls from several host threads are well defined (they
     // compute the same value)
@@ -515,9 +533,9 @@ int strip_occupancy(int dev, int nstage) {
     const size_t smem = Cfg::smem_bytes(nstage);
     int per_sm = 0;
     if (smem <= 232448 &&
-        cudaFuncSetAttribute(strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM>,
+        cudaFuncSetAttribute(strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM, VN>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) == cudaSuccess &&
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM>,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, strip_scan_kernel<K, Tin, Te, LPR, SR, SUMM, VN>,
                                                       Cfg::NT, smem) == cudaSuccess &&
         per_sm > 0) {
         slot.store(per_sm, std::memory_order_relaxed);
@@ -535,7 +553,7 @@ int strip_occupancy(int dev, int nstage) {
 // (strips over SMs in one wave, or waves over the resident CTAs) x 0.6 when
 // SMs would hold a single CTA x a short-row penalty (0.97 for 128-byte rows,
 // 0.9 for 64-byte rows); ties go to the wider strip.  Stages: two (see below).
-template <Kind K, typename Tin, typename Te, int SR4, int SR8, int SR16, int SR32, bool SUMM = false>
+template <Kind K, typename Tin, typename Te, int SR4, int SR8, int SR16, int SR32, bool SUMM = false, int NSR = 0>
 int strip_launch_kind(const ScanCall& call, bool* taken) {
     *taken = false;
     int dev = 0;
@@ -545,6 +563,30 @@ int strip_launch_kind(const ScanCall& call, bool* taken) {
     const int64_t T = call.a.T, nb = call.a.nb * (call.npiece > 1 ? call.npiece : 1), hd = call.a.hd;
     using P = Policy<K, Tin, Te>;
     if (T < 16) return ESA_OK;
+    // narrow form (NSR > 0, float accumulators): 64-channel strips of 32
+    // two-channel lanes, one row group a warp and NSR steps a thread -- no
+    // shuffle scan across row groups, the CTA prefix amortised over NSR steps
+    // (the [16, 2048, 768] fp16 gated forward: 2.03 -> 2.76 TB/s against the
+    // 8-channel lanes); taken whenever its strips fill the GPU
+    if constexpr (NSR > 0 && std::is_same<typename Policy<K, Tin, Te, 2>::acc, float>::value) {
+        const int64_t n = nb * ((hd + 63) / 64);
+        if (n >= (sms * 3) / 4) {
+            int ns = 0, o = 0;
+            for (int s = 2; s <= 6; ++s) {
+                const int os = strip_occupancy<K, Tin, Te, 32, NSR, SUMM, 2>(dev, s);
+                if (os > o) {
+                    o = os;
+                    ns = s;
+                }
+                if (o >= 2) break;
+            }
+            if (o > 0) {
+                *taken = true;
+                const int64_t cap = (int64_t)o * sms;
+                return strip_launch_typed<K, Tin, Te, 32, NSR, SUMM, 2>(call, ns, (int)(n < cap ? n : cap));
+            }
+        }
+    }
     auto strips = [&](int lpr) { return nb * ((hd + lpr * P::VEC - 1) / (lpr * P::VEC)); };
     auto occ = [&](int lpr, int ns) -> int {
         switch (lpr) {

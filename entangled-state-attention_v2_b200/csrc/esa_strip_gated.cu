@@ -7,10 +7,15 @@
 namespace esa {
 
 namespace {
+// steps a thread in the narrow form: 128-step tiles; its A, B register cache
+// holds 16 x 2 x 2 values
+constexpr int kNarrowSteps = 16;
+
 template <typename Tin, typename Te>
 int go(const ScanCall& c, bool* taken) {
-    // two steps per row group keep the A/B register cache at 2*VEC*2 values
-    return strip_launch_kind<Kind::FwdGated, Tin, Te, 1, 2, 2, 2>(c, taken);
+    // wide form: two steps per row group keep the A/B register cache at
+    // 2*VEC*2 values
+    return strip_launch_kind<Kind::FwdGated, Tin, Te, 1, 2, 2, 2, false, kNarrowSteps>(c, taken);
 }
 }  // namespace
 

@@ -6,9 +6,13 @@
 namespace esa {
 
 namespace {
+// steps a thread in the narrow form: 64-step tiles (four staged arrays, 32 KB
+// a 16-bit stage)
+constexpr int kNarrowSteps = 8;
+
 template <typename Tin, typename Te>
 int go(const ScanCall& c, bool* taken) {
-    return strip_launch_kind<Kind::RevGated, Tin, Te, 1, 2, 2, 2>(c, taken);
+    return strip_launch_kind<Kind::RevGated, Tin, Te, 1, 2, 2, 2, false, kNarrowSteps>(c, taken);
 }
 }  // namespace
 

@@ -121,12 +121,12 @@ def check(rc: int, what: str) -> None:
     raise RuntimeError(f"{what} failed ({rc}): {msg}")
 
 
-SCAN_PATHS = {0: "none", 1: "sequential", 2: "lookback", 3: "strip", 4: "lane", 5: "rowtile"}
+SCAN_PATHS = {0: "none", 1: "sequential", 2: "lookback", 3: "strip", 4: "lane"}
 
 
 def last_scan_path() -> str:
     """Kernel family of the last scan launch on this host thread: "sequential",
-    "lookback", "strip", "lane" or "rowtile" ("none" before any)."""
+    "lookback", "strip" or "lane" ("none" before any)."""
     return SCAN_PATHS.get(int(lib().esa_scan_last_path()), "unknown")
 
 

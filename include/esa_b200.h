@@ -152,16 +152,13 @@ int esa_cross_entropy_bwd(const void *logits, int64_t row_stride, int dtype, con
  * channel, any alignment), ESA_PATH_LOOKBACK (time chunks, decoupled
  * look-back), ESA_PATH_STRIP (channel strips, tile-parallel steps),
  * ESA_PATH_LANE (channel strips, one lane per channel vector walking the
- * steps in order), ESA_PATH_ROWTILE (tiles of a few steps x all channels of
- * a batch row, decoupled look-back: the fused layer core and the gated
- * scans).  A split scan reports its output pass.  No reference
+ * steps in order).  A split scan reports its output pass.  No reference
  * counterpart. */
 #define ESA_PATH_NONE 0
 #define ESA_PATH_SEQUENTIAL 1
 #define ESA_PATH_LOOKBACK 2
 #define ESA_PATH_STRIP 3
 #define ESA_PATH_LANE 4
-#define ESA_PATH_ROWTILE 5
 int esa_scan_last_path(void);
 
 /* Version of this ABI (ESA_ABI_VERSION). */
@@ -297,17 +294,13 @@ int esa_gated_scan_bwd(const void *gate_raw, const void *value_raw, int64_t raw_
                        void *workspace, size_t workspace_bytes, void *stream);
 
 /* Workspace (bytes) of esa_layer_fwd / esa_layer_bwd for [nb, T, C] with
- * these dtypes: look-back descriptors and flags of the fused kernel, or, for
- * shapes and dtype mixes it does not cover, the gated scan's workspace plus
- * the dE buffer of the two-kernel backward.  Sized for operands whose rows
- * are 16-byte aligned (contiguous PyTorch tensors with C*esize a multiple of
- * 16); with unaligned operands the calls take the two-kernel form and may
- * report ESA_ERR_WORKSPACE.  0 for invalid arguments.  No counterpart in the
- * reference (it has no native code). */
+ * these dtypes: the gated scan's workspace plus the dE buffer between the
+ * readout backward and the reverse scan.  0 for invalid arguments.  No
+ * counterpart in the reference (it has no native code). */
 size_t esa_layer_workspace_bytes(int64_t nb, int64_t T, int64_t C, int qgv_dtype, int e_dtype,
                                  int y_dtype);
 
-/* The ESA layer core forward, fused: from the qgv projection [nb, T, 3C]
+/* The ESA layer core forward: from the qgv projection [nb, T, 3C]
  * (q | gate_raw | value_raw; rows `qgv_row_stride` elements apart, of
  * qgv_dtype) it computes
  *   A = gmin + (gmax - gmin) sigmoid(gate_raw),  B = (1 - A) tanh(value_raw)
@@ -316,12 +309,9 @@ size_t esa_layer_workspace_bytes(int64_t nb, int64_t T, int64_t C, int qgv_dtype
  *   y = sigmoid(q) * E * rsqrt(mean_C(E^2) + eps)
  * writing E ([nb, T, C] of e_dtype, kept for the backward), y ([nb, T, C] of
  * y_dtype), rstd ([nb*T], acc type: the per-row rsqrt) and, if not NULL,
- * e_last = E_{T-1} (acc [nb, C]).  Where the shape and dtypes allow (C a
- * multiple of 64 up to 768, or of 128 up to 1536; 16-bit throughout, fp32
- * throughout, or fp32 qgv / y with a 16-bit scan) one kernel reads qgv once
- * and writes E and y once: tiles of a few steps x all C channels of a batch
- * row, chained through a decoupled look-back; otherwise the gated scan and
- * the readout run in turn.  Replaces ThunderESA.forward from the qgv
+ * e_last = E_{T-1} (acc [nb, C]).  Two launches on `stream`: the gated scan
+ * (gates fused into the scan's loads) and the RMS readout (sigmoid(q) gate
+ * fused).  Replaces ThunderESA.forward from the qgv
  * projection to the out_proj input (esa/backends/thunder.py:275-311: split,
  * gates, cast, thunder_scan, RMS readout, sigmoid(q) gate). */
 int esa_layer_fwd(const void *qgv, int64_t qgv_row_stride, int qgv_dtype, void *E, int e_dtype,
@@ -329,7 +319,7 @@ int esa_layer_fwd(const void *qgv, int64_t qgv_row_stride, int qgv_dtype, void *
                   double gate_min, double gate_max, double eps, const void *e0, void *e_last,
                   void *workspace, size_t workspace_bytes, void *stream);
 
-/* Backward of esa_layer_fwd, fused: from dy ([nb, T, C] of dy_dtype), qgv,
+/* Backward of esa_layer_fwd: from dy ([nb, T, C] of dy_dtype), qgv,
  * E and rstd it writes d qgv ([nb, T, 3C] of qgv_dtype, rows
  * `dqgv_row_stride` apart):
  *   dq = dy n s (1 - s),  dE = r (dy s - n mean_C(dy s n))   (s = sigmoid(q),
@@ -337,8 +327,9 @@ int esa_layer_fwd(const void *qgv, int64_t qgv_row_stride, int qgv_dtype, void *
  *   d gate_raw = (G E_{t-1} - G tanh v) (gmax - gmin) s_g (1 - s_g),
  *   d value_raw = G (1 - A)(1 - tanh^2 v),
  * with E_{-1} = e0 (NULL: zero) and de0 (nullable) = A_0 G_0, the gradient
- * w.r.t. e0.  One kernel where esa_layer_fwd uses one, else the readout
- * backward and the gated reverse scan in turn.  Replaces the autograd of
+ * w.r.t. e0.  Two launches: the readout backward (writes dq and dE into the
+ * workspace) and the gated reverse scan (gate chain rule fused).  Replaces
+ * the autograd of
  * esa/backends/thunder.py:275-311. */
 int esa_layer_bwd(const void *dy, int dy_dtype, const void *qgv, int64_t qgv_row_stride,
                   int qgv_dtype, const void *E, int e_dtype, const void *rstd, void *dqgv,

@@ -253,20 +253,19 @@ def test_seeded_weights_cover_the_model_fixtures():
 
 
 def test_layer_core_entry_points_need_no_gpu_for_sizes_and_errors():
-    """esa_layer_workspace_bytes is host arithmetic (the fused kernel's
-    look-back descriptors, or the two-kernel form's scan workspace plus its dE
-    buffer); esa_layer_fwd / esa_layer_bwd reject bad arguments before any
+    """esa_layer_workspace_bytes is host arithmetic (the gated scan's
+    workspace plus the dE buffer between the readout backward and the reverse
+    scan); esa_layer_fwd / esa_layer_bwd reject bad arguments before any
     device work."""
     from esa import _lib
     L = _lib.lib()
     F16, F32 = _lib.DTYPE_F16, _lib.DTYPE_F32
-    fused = L.esa_layer_workspace_bytes(16, 2048, 768, F16, F16, F16)
-    # tiles of 8 steps x 768 channels (the backward's): three fp32 planes
-    ntiles = 16 * 2048 // 8
-    assert fused >= 3 * ntiles * 768 * 4
-    assert fused < 4 * ntiles * 768 * 4
-    two_kernel = L.esa_layer_workspace_bytes(2, 300, 96, F32, F32, F32)  # C not a multiple of 64
-    assert two_kernel >= 2 * 300 * 96 * 4                                # holds dE
+    ws = L.esa_layer_workspace_bytes(16, 2048, 768, F16, F16, F16)
+    scan = L.esa_scan_workspace_bytes(16, 2048, 768, F16, 16)
+    de = 16 * 2048 * 768 * 2
+    assert ws == de + scan
+    two = L.esa_layer_workspace_bytes(2, 300, 96, F32, F32, F32)
+    assert two >= 2 * 300 * 96 * 4                                # holds dE
     assert L.esa_layer_workspace_bytes(2, 300, 96, 9, F32, F32) == 0
     assert L.esa_layer_workspace_bytes(2, 300, 0, F32, F32, F32) == 0
     rc = L.esa_layer_fwd(None, 100, F16, None, F16, None, F16, None, 2, 8, 64, 0.8, 0.995, 1e-5,

@@ -178,6 +178,43 @@ def test_gated_scan_training_layer_shape():
     assert rel(dv[rows], dv_ref) < 4e-3
 
 
+@pytest.mark.parametrize("raw_dtype,scan_dtype", [
+    (torch.float16, torch.float16), (torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32),
+    (torch.float32, torch.float16), (torch.float32, torch.bfloat16), (torch.float16, torch.float32),
+    (torch.bfloat16, torch.float32)])
+@pytest.mark.parametrize("nb,T,C", [(4, 300, 2048), (8, 777, 1000)])
+def test_gated_narrow_strip_scan(raw_dtype, scan_dtype, nb, T, C):
+    """The narrow strip form (64-channel strips of 32 two-channel lanes),
+    which the gated scans take whenever their 64-channel strips fill the GPU
+    (here 128 strips): ragged last tiles (T = 300, 777), a last strip with 40
+    of 64 channels (C = 1000), an initial state, the final state and its
+    gradient -- against the oracle on the same rounded A, B."""
+    from esa import _lib, ops
+    g = torch.Generator().manual_seed(T + C)
+    qgv = torch.randn(nb, T, 3 * C, generator=g).to(raw_dtype)
+    gr, vr = qgv[..., C:2 * C], qgv[..., 2 * C:]
+    qd = qgv.to(DEV)
+    grd, vrd = qd[..., C:2 * C], qd[..., 2 * C:]
+    e0 = torch.randn(nb, C, generator=g)
+    E, e_last = ops.gated_scan(grd, vrd, e0.to(DEV), 0.8, 0.995, 16, scan_dtype)
+    assert _lib.last_scan_path() in ("strip", "lane")  # lane: ESA_SCAN_PATH=lane
+    A64, B64 = oracle.gate(gr, vr)
+    Ar = torch.from_numpy(A64).to(scan_dtype).double().reshape(nb, T, 1, C)
+    Br = torch.from_numpy(B64).to(scan_dtype).double().reshape(nb, T, 1, C)
+    ref = oracle.scan_fwd(Ar, Br, e0=e0.double()).reshape(nb, T, C)
+    tol = max(TOL[scan_dtype], TOL[raw_dtype])
+    assert rel(E, ref) < tol
+    assert rel(e_last, ref[:, -1]) < tol
+    dE = torch.randn(nb, T, C, generator=g).to(scan_dtype)
+    dg, dv, de0 = ops.gated_scan_backward(grd, vrd, E, dE.to(DEV), e0.to(DEV), 0.8, 0.995, 16)
+    dA, dB, de0_ref = oracle.scan_rev(Ar, E.double().cpu().reshape(nb, T, 1, C), dE.double().reshape(nb, T, 1, C),
+                                      e0=e0.double())
+    dg_ref, dv_ref = oracle.gate_bwd(gr, vr, dA.reshape(nb, T, C), dB.reshape(nb, T, C))
+    assert rel(dg, dg_ref) < tol * 2
+    assert rel(dv, dv_ref) < tol * 2
+    assert rel(de0, de0_ref.reshape(nb, C)) < tol
+
+
 def test_gated_autograd_through_layer_slices():
     """torch autograd through the gated op equals autograd through the
     materialised gate + thunder_scan (both on the GPU, fp64)."""
