@@ -553,7 +553,8 @@ int strip_occupancy(int dev, int nstage) {
 // (strips over SMs in one wave, or waves over the resident CTAs) x 0.6 when
 // SMs would hold a single CTA x a short-row penalty (0.97 for 128-byte rows,
 // 0.9 for 64-byte rows); ties go to the wider strip.  Stages: two (see below).
-template <Kind K, typename Tin, typename Te, int SR4, int SR8, int SR16, int SR32, bool SUMM = false, int NSR = 0>
+template <Kind K, typename Tin, typename Te, int SR4, int SR8, int SR16, int SR32, bool SUMM = false, int NSR = 0,
+          int NVN = 2>
 int strip_launch_kind(const ScanCall& call, bool* taken) {
     *taken = false;
     int dev = 0;
@@ -563,17 +564,18 @@ int strip_launch_kind(const ScanCall& call, bool* taken) {
     const int64_t T = call.a.T, nb = call.a.nb * (call.npiece > 1 ? call.npiece : 1), hd = call.a.hd;
     using P = Policy<K, Tin, Te>;
     if (T < 16) return ESA_OK;
-    // narrow form (NSR > 0, float accumulators): 64-channel strips of 32
-    // two-channel lanes, one row group a warp and NSR steps a thread -- no
-    // shuffle scan across row groups, the CTA prefix amortised over NSR steps
-    // (the [16, 2048, 768] fp16 gated forward: 2.03 -> 2.76 TB/s against the
-    // 8-channel lanes); taken whenever its strips fill the GPU
-    if constexpr (NSR > 0 && std::is_same<typename Policy<K, Tin, Te, 2>::acc, float>::value) {
-        const int64_t n = nb * ((hd + 63) / 64);
+    // narrow form (NSR > 0, float accumulators): strips of 32 lanes of NVN
+    // channels, one row group a warp and NSR steps a thread -- no shuffle
+    // scan across row groups, the CTA prefix amortised over NSR steps (the
+    // [16, 2048, 768] fp16 gated forward: 2.03 -> 2.76 TB/s against 8-channel
+    // lanes; the [32, 4096, 16, 64] fp16 plain reverse with 4-channel lanes:
+    // 5.59 -> 6.07 TB/s); taken whenever its strips fill the GPU
+    if constexpr (NSR > 0 && std::is_same<typename Policy<K, Tin, Te, NVN>::acc, float>::value) {
+        const int64_t n = nb * ((hd + 32 * NVN - 1) / (32 * NVN));
         if (n >= (sms * 3) / 4) {
             int ns = 0, o = 0;
             for (int s = 2; s <= 6; ++s) {
-                const int os = strip_occupancy<K, Tin, Te, 32, NSR, SUMM, 2>(dev, s);
+                const int os = strip_occupancy<K, Tin, Te, 32, NSR, SUMM, NVN>(dev, s);
                 if (os > o) {
                     o = os;
                     ns = s;
@@ -583,7 +585,7 @@ int strip_launch_kind(const ScanCall& call, bool* taken) {
             if (o > 0) {
                 *taken = true;
                 const int64_t cap = (int64_t)o * sms;
-                return strip_launch_typed<K, Tin, Te, 32, NSR, SUMM, 2>(call, ns, (int)(n < cap ? n : cap));
+                return strip_launch_typed<K, Tin, Te, 32, NSR, SUMM, NVN>(call, ns, (int)(n < cap ? n : cap));
             }
         }
     }

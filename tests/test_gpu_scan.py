@@ -117,6 +117,33 @@ def test_initial_state_and_final_state(dtype):
     assert rel(Ad.grad, dA_ref) < TOL[dtype]
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(16, 300, 8, 128), (16, 129, 8, 125)])
+def test_scan_backward_narrow_strips(dtype, shape):
+    """16-bit reverse scans on 128-channel strips of four-channel lanes (taken
+    when those strips fill the GPU; here 128 of them): a ragged last tile
+    (T = 300, 129), a last strip with 104 of 128 channels (hd = 1000), and
+    the gradient w.r.t. an initial state."""
+    from esa import _lib, ops
+    g = torch.Generator().manual_seed(shape[1])
+    nb, T, H, D = shape
+    A = torch.sigmoid(torch.randn(shape, generator=g) + 3).to(dtype)
+    B = torch.randn(shape, generator=g).to(dtype)
+    e0 = torch.randn(nb, H * D, generator=g).to(dtype)
+    dE = torch.randn(shape, generator=g).to(dtype)
+    Ad = A.to(DEV).requires_grad_(True)
+    Bd = B.to(DEV).requires_grad_(True)
+    e0d = e0.to(DEV).requires_grad_(True)
+    E, _ = ops.scan(Ad, Bd, e0d, 16)
+    E.backward(dE.to(DEV))
+    assert _lib.last_scan_path() in ("strip", "lane")  # lane: ESA_SCAN_PATH=lane
+    dA_ref, dB_ref, de0_ref = oracle.scan_rev(A.double(), E.detach().double().cpu(), dE.double(),
+                                              e0=e0.double())
+    assert rel(Bd.grad, dB_ref) < TOL[dtype]
+    assert rel(Ad.grad, dA_ref) < TOL[dtype]
+    assert rel(e0d.grad, de0_ref.reshape(nb, H * D)) < TOL[dtype]
+
+
 @pytest.mark.parametrize("raw_dtype,scan_dtype", [
     (torch.float32, torch.float32), (torch.float32, torch.float16), (torch.float16, torch.float16),
     (torch.bfloat16, torch.bfloat16), (torch.float16, torch.float32), (torch.float64, torch.float64),
