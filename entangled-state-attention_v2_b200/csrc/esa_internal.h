@@ -85,6 +85,13 @@ struct ScanCall {
 // Channel-strip scan (no inter-CTA waits).  Sets *taken = false when the
 // problem has too few channels to fill the GPU with strips.
 int strip_scan_launch(const ScanCall& c, bool* taken);
+// Single-pass chained scan of time pieces (esa_chain.cu): the plain forward
+// scan of few channels over a long time axis.  Sets *taken = false when the
+// shape is not one it serves or the workspace is smaller than
+// chain_workspace_bytes.
+int chain_scan_launch(const ScanCall& c, bool* taken);
+size_t chain_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int es);
+bool chain_applies_dims(int64_t nb, int64_t T, int64_t hd, int es);
 // Time-chunked scan with decoupled lookback (any shape with aligned rows).
 int lookback_scan_launch(const ScanCall& c);
 // Sequential per-channel scan (any shape, any alignment).

@@ -293,6 +293,11 @@ int run(ScanCall& c) {
     c.a.status = status_ptr(dev);
     if (c.a.status == nullptr) return set_error(ESA_ERR_CUDA, "cannot resolve the device status word");
     if (!c.bulk_ok) return sequential_scan_launch(c);
+    {
+        bool chained = false;
+        if (int rc = chain_scan_launch(c, &chained)) return rc;
+        if (chained) return ESA_OK;
+    }
     bool done = false;
     if (int rc = run_split(c, &done)) return rc;
     if (done) return ESA_OK;
@@ -461,7 +466,9 @@ size_t scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int 
     const size_t lb = lookback_workspace_bytes(nb, T, hd, wide_es, compass);
     const SplitPlan sp = split_plan(nb, T, hd, wide_es);
     const size_t split = sp.npiece > 1 ? 3 * split_plane_bytes(nb, sp, hd, wide_es == 8 ? 8 : 4) : 0;
-    return lb > split ? lb : split;
+    const size_t chain = chain_workspace_bytes(nb, T, hd, wide_es);
+    const size_t m = lb > split ? lb : split;
+    return m > chain ? m : chain;
 }
 
 int scan_fwd(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd, int dtype,

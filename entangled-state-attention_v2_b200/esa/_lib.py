@@ -121,7 +121,7 @@ def check(rc: int, what: str) -> None:
     raise RuntimeError(f"{what} failed ({rc}): {msg}")
 
 
-SCAN_PATHS = {0: "none", 1: "sequential", 2: "lookback", 3: "strip", 4: "lane"}
+SCAN_PATHS = {0: "none", 1: "sequential", 2: "lookback", 3: "strip", 4: "lane", 5: "chain"}
 
 
 def last_scan_path() -> str:

@@ -152,13 +152,15 @@ int esa_cross_entropy_bwd(const void *logits, int64_t row_stride, int dtype, con
  * channel, any alignment), ESA_PATH_LOOKBACK (time chunks, decoupled
  * look-back), ESA_PATH_STRIP (channel strips, tile-parallel steps),
  * ESA_PATH_LANE (channel strips, one lane per channel vector walking the
- * steps in order).  A split scan reports its output pass.  No reference
- * counterpart. */
+ * steps in order), ESA_PATH_CHAIN (time pieces chained by a single-pass
+ * look-back, each piece read from HBM once and re-read from L2).  A split
+ * scan reports its output pass.  No reference counterpart. */
 #define ESA_PATH_NONE 0
 #define ESA_PATH_SEQUENTIAL 1
 #define ESA_PATH_LOOKBACK 2
 #define ESA_PATH_STRIP 3
 #define ESA_PATH_LANE 4
+#define ESA_PATH_CHAIN 5
 int esa_scan_last_path(void);
 
 /* Version of this ABI (ESA_ABI_VERSION). */

@@ -3,9 +3,11 @@
 With few channels per batch row the strips cannot fill the GPU, so the time
 axis is cut across CTAs: below 8192 steps by the time-parallel look-back scan
 (per-tile aggregates, a decoupled look-back over earlier tiles, outputs from
-the exact incoming state), from 8192 steps by the split scan (time pieces as
-strip rows: summary pass, composition of the pieces' incoming states, output
-pass).  These shapes (a few strips' worth of channels, thousands of steps)
+the exact incoming state), from 8192 steps by the single-pass chained scan
+(plain forward of 16- and 32-bit data: time pieces read once, chained by a
+per-warp look-back, re-read from L2 for the outputs) or the split scan (every
+other kind: time pieces as strip rows, summary pass, composition of the
+pieces' incoming states, output pass).  These shapes (a few strips' worth of channels, thousands of steps)
 exercise both in every kind, with initial and final states, and the host
 pipeline's time pieces.
 Same bar as the other scan tests: relative Frobenius error against the fp64
@@ -63,6 +65,29 @@ def test_chained_forward_with_states(dtype, shape):
     assert rel(E0, oracle.scan_fwd(A.double(), B.double())) < TOL[dtype]
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(2, 8192, 2, 64), (1, 12345, 3, 32), (2, 9000, 3, 64), (3, 20000, 1, 8)])
+def test_single_pass_chained_scan(dtype, shape):
+    """The plain forward of few channels over >= 8192 steps runs the
+    single-pass chained kernel: with an initial state, a ragged last piece and
+    last tile (T = 12345, 9000, 20000), a partial last strip (96 and 192
+    channels against 128-channel strips, 8 against 64) and several batch rows."""
+    from esa import _lib, ops
+    A, B, g = _inputs(shape, dtype, 21)
+    nb, T, H, D = shape
+    e0 = torch.randn(nb, H * D, generator=g, dtype=torch.float64).float()
+    E, e_last = ops.scan(A.to(DEV), B.to(DEV), e0.to(DEV), 16)
+    assert _lib.last_scan_path() == "chain"
+    ref = oracle.scan_fwd(A.double(), B.double(), e0=e0.double())
+    assert rel(E, ref) < TOL[dtype]
+    assert rel(e_last, ref[:, -1].reshape(nb, H * D)) < TOL[dtype]
+    # a second call (tickets and flags reset per launch) agrees to rounding:
+    # how many predecessor aggregates a look-back composes before it meets an
+    # inclusive prefix depends on timing, so the last bits may differ
+    E2, _ = ops.scan(A.to(DEV), B.to(DEV), e0.to(DEV), 16)
+    assert rel(E2, E.double().cpu().numpy()) < TOL[dtype] / 10
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float64])
 def test_chained_reverse_with_states(dtype):
     from esa import ops
@@ -111,16 +136,18 @@ def test_chained_gated_fwd_bwd(raw_dtype, scan_dtype):
 
 
 def test_chained_long_sequence_properties():
-    """Long-sequence size [4, 262144, 32, 64] bf16: sampled channels against the
-    oracle (fp64 on the same rounded inputs) and the end state against the
-    slice-summary composition (size-independent checks)."""
-    from esa import ops
+    """Long-sequence size [4, 262144, 32, 64] bf16 (the single-pass chained
+    kernel): sampled channels against the oracle (fp64 on the same rounded
+    inputs) and the end state against the slice summary, which the split
+    summary pass computes on its own (size-independent checks)."""
+    from esa import _lib, ops
     torch.manual_seed(0)
     shp = (4, 262144, 32, 64)
     dev = torch.device(DEV)
     A = torch.sigmoid(torch.randn(shp, device=dev) + 3).to(torch.bfloat16)
     B = (torch.randn(shp, device=dev) * 0.5).to(torch.bfloat16)
     E, e_last = ops.scan(A, B, None, 16)
+    assert _lib.last_scan_path() == "chain"
     # channels of two heads of rows 0 and 3, over the first and the last 4096 steps
     for rows in (slice(0, 1), slice(3, 4)):
         for ts in (slice(0, 4096), slice(shp[1] - 4096, shp[1])):

@@ -232,9 +232,9 @@ def test_sequence_parallel_scan_nccl():
 @pytest.mark.gpu
 @pytest.mark.parametrize("shape", [(4, 16384, 32, 64), (2, 300, 4, 64)])
 def test_summary_then_resume_equals_full_scan(shape):
-    """esa_scan_fwd_resume after esa_scan_summary on the same workspace gives
-    the bits of esa_scan_fwd (split slices reuse the piece summaries; short
-    slices are scanned in full)."""
+    """esa_scan_fwd_resume after esa_scan_summary on the same workspace agrees
+    with esa_scan_fwd (split slices reuse the piece summaries; short slices
+    are scanned in full)."""
     from esa import _lib, ops
     torch.manual_seed(2)
     A = torch.sigmoid(torch.randn(shape, device="cuda") + 3).to(torch.bfloat16)
@@ -257,14 +257,10 @@ def test_summary_then_resume_equals_full_scan(shape):
                                      e0.data_ptr(), e_last.data_ptr(), ws.data_ptr(), ws.numel(), s),
                "resume")
     torch.cuda.synchronize()
-    if T >= 8192:
-        # split slice: the same deterministic passes, the same bits
-        assert torch.equal(E, ref)
-        assert torch.equal(e_last, ref_last)
-    else:
-        # scanned in full by the time-parallel kernel, whose association
-        # order may differ from call to call
-        torch.testing.assert_close(E.float(), ref.float(), rtol=1e-2, atol=1e-2)
-        torch.testing.assert_close(e_last, ref_last, rtol=1e-5, atol=1e-5)
+    # esa_scan_fwd takes a time-parallel kernel (the single-pass chained scan
+    # from 8192 steps, the look-back scan below) whose association order
+    # differs from the split passes': equal to rounding
+    torch.testing.assert_close(E.float(), ref.float(), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(e_last, ref_last, rtol=1e-5, atol=1e-5)
     # the slice summary composes with e0 into the end state
     torch.testing.assert_close(prod * e0 + e_end, e_last, rtol=1e-4, atol=1e-5)
