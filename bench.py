@@ -190,27 +190,29 @@ class Ctx:
             self.dist.destroy_process_group()
 
 
-def _timed(ctx, fn, steps: int, stream=None) -> tuple[float, list[float], dict]:
-    """Run fn() `steps` times between CUDA events on the launching stream,
-    barrier + synchronize on both sides, clocks sampled meanwhile.  Returns
-    (max-over-ranks total ms, this rank's per-step ms, clocks)."""
+def _timed(ctx, fn, steps: int, stream=None) -> tuple[float, float, dict]:
+    """Run fn() `steps` times back to back between two CUDA events on the
+    launching stream (an event between steps would add its own gap to every
+    step), barrier + synchronize on both sides, clocks sampled meanwhile.
+    Returns (max-over-ranks total ms, this rank's mean ms per step, clocks)."""
     import torch
     stream = stream or torch.cuda.current_stream(ctx.dev)
     clocks = ClockSampler(ctx.local).start()
     time.sleep(0.3)
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
-    ev[0].record(stream)
-    for i in range(steps):
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
         fn()
-        ev[i + 1].record(stream)
+    ev1.record(stream)
     torch.cuda.synchronize(ctx.dev)
     ctx.barrier()
     clk = clocks.stop()
-    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
-    total = ctx.max_over_ranks(ev[0].elapsed_time(ev[-1]))
-    return total, per, clk
+    mine = ev0.elapsed_time(ev1)
+    total = ctx.max_over_ranks(mine)
+    return total, mine / steps, clk
 
 
 # ---------------------------------------------------------------------------
@@ -341,10 +343,9 @@ def scan_leg(ctx) -> dict:
         step()
     torch.cuda.synchronize(dev)
     path = _lib.last_scan_path()  # kernel family the timed launches use
-    total_ms, per, clk = _timed(ctx, step, args.steps, stream)
+    total_ms, mean_launch_ms, clk = _timed(ctx, step, args.steps, stream)
     alg_bytes = 3 * N * 2
     value = ws * alg_bytes * args.steps / (total_ms * 1e-3) / 1e9
-    mean_launch_ms = statistics.mean(per)
     peak, peak_kind = _peaks()
     achieved = alg_bytes / (mean_launch_ms * 1e-3) / 1e9
     ops.check_device_status(dev)
@@ -602,7 +603,7 @@ def train_leg(ctx) -> dict:
     for _ in range(warm):
         step()
     torch.cuda.synchronize(dev)
-    total_ms, per, clk = _timed(ctx, step, steps)
+    total_ms, _, clk = _timed(ctx, step, steps)
     ops.check_device_status(dev)
     tok = ws * B * T * steps / (total_ms * 1e-3)
     peak, kind = _bf16_peak()
