@@ -878,7 +878,7 @@ def comparators_leg(timeout_s: int = 420) -> dict:
 # four iterations of one kernel family, so a profiler can skip the first
 # launches and capture one
 # ---------------------------------------------------------------------------
-PROFILE_WORKLOADS = ("rev", "gated", "long", "readout", "layer", "layernorm", "train")
+PROFILE_WORKLOADS = ("rev", "gated", "long", "readout", "layer", "layernorm", "train", "decode")
 
 
 def profile_workload(name: str, iters: int = 4) -> None:
@@ -928,6 +928,24 @@ def profile_workload(name: str, iters: int = 4) -> None:
         print(f"device time per step: {total / 2:.1f} us")
         for t, n, key in rows[:30]:
             print(f"{t / 2:10.1f} us {100 * t / total:5.1f} % {n // 2:4d} launches  {key[:100]}")
+        return
+    if name == "decode":
+        # eager batch-1 decode steps of the 24-layer / 1024-wide fp16 model
+        from esa import ESAModel, ESAModelConfig
+        torch.manual_seed(1234)
+        cfg = ESAModelConfig(vocab_size=32000, n_layer=24, embd=1024, head=16, block=1024, dropout=0.0,
+                             precision="fp16")
+        model = ESAModel(cfg, device="cuda").eval().half()
+        token = torch.zeros(1, dtype=torch.long, device=dev)
+        states = torch.zeros(24, 1, 16, 64, dtype=torch.float16, device=dev)
+        pos = torch.tensor(3, device=dev)
+        with torch.inference_mode():
+            for _ in range(iters):
+                logits, states = model.lightning_step(token, states, pos)
+                token = torch.argmax(logits, dim=-1)
+        torch.cuda.synchronize()
+        ops.check_device_status()
+        print("ok", name)
         return
     if name == "rev":
         A = torch.sigmoid(rnd(32, 4096, 16, 64, dtype=torch.float32) * 2 + 2).half()

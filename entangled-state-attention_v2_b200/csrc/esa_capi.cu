@@ -258,4 +258,55 @@ ESA_EXPORT int esa_lightning_step(const void* qgv, int64_t qgv_row_stride, int q
                           nb, C, gate_min, gate_max, eps, static_cast<cudaStream_t>(stream));
 }
 
+ESA_EXPORT size_t esa_decode_block_scratch_bytes(int64_t nb, int64_t C, int dtype) {
+    return decode_block_scratch_bytes(nb, C, dtype);
+}
+
+ESA_EXPORT int esa_decode_block(const void* x, const void* pending, void* x_out, void* pending_out,
+                                const void* state, void* new_state, const void* ln1_w, const void* ln1_b,
+                                const void* qgv_w, const void* qgv_b, const void* out_w, const void* out_b,
+                                const void* ln2_w, const void* ln2_b, const void* fc_w, const void* fc_b,
+                                const void* proj_w, const void* proj_b, int64_t nb, int64_t C, int dtype,
+                                double gate_min, double gate_max, double eps, double ln_eps, void* scratch,
+                                size_t scratch_bytes, void* stream) {
+    clear_error();
+    DecodeBlock p{};
+    p.x = x;
+    p.pending = pending;
+    p.x_out = x_out;
+    p.pending_out = pending_out;
+    p.state = state;
+    p.new_state = new_state;
+    p.ln1_w = ln1_w;
+    p.ln1_b = ln1_b;
+    p.qgv_w = qgv_w;
+    p.qgv_b = qgv_b;
+    p.out_w = out_w;
+    p.out_b = out_b;
+    p.ln2_w = ln2_w;
+    p.ln2_b = ln2_b;
+    p.fc_w = fc_w;
+    p.fc_b = fc_b;
+    p.proj_w = proj_w;
+    p.proj_b = proj_b;
+    p.scratch = scratch;
+    p.scratch_bytes = scratch_bytes;
+    p.nb = nb;
+    p.C = C;
+    p.dtype = dtype;
+    p.gate_min = gate_min;
+    p.gate_max = gate_max;
+    p.eps = eps;
+    p.ln_eps = ln_eps;
+    return decode_block(p, static_cast<cudaStream_t>(stream));
+}
+
+ESA_EXPORT int esa_decode_head(const void* x, const void* pending, const void* ln_w, const void* ln_b,
+                               double ln_eps, const void* W, const void* bias, void* logits, int64_t nb, int64_t C,
+                               int64_t V, int dtype, void* stream) {
+    clear_error();
+    return decode_head(x, pending, ln_w, ln_b, ln_eps, W, bias, logits, nb, C, V, dtype,
+                       static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

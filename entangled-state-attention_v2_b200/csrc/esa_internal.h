@@ -150,4 +150,25 @@ int lightning_step(const void* qgv, int64_t qrs, int qdt, const void* state, voi
                    int sdt, void* z, int zdt, int64_t nb, int64_t C, double gmin, double gmax,
                    double eps, cudaStream_t s);
 
+// ESAModel block decode step for a few rows of 16-bit data (esa_decode.cu).
+constexpr int kDecodeMaxRows = 4;
+struct DecodeBlock {
+    const void *x, *pending;            // [nb, C]; pending nullable (first block)
+    void *x_out, *pending_out;          // [nb, C]
+    const void* state;                  // [nb, C]
+    void* new_state;                    // [nb, C], not aliasing state
+    const void *ln1_w, *ln1_b, *qgv_w, *qgv_b, *out_w, *out_b;
+    const void *ln2_w, *ln2_b, *fc_w, *fc_b, *proj_w, *proj_b;  // biases nullable
+    void* scratch;
+    size_t scratch_bytes;
+    int64_t nb, C;
+    int dtype;
+    double gate_min, gate_max, eps, ln_eps;
+};
+size_t decode_block_scratch_bytes(int64_t nb, int64_t C, int dtype);
+int decode_block(const DecodeBlock& p, cudaStream_t s);
+int decode_head(const void* x, const void* pending, const void* ln_w, const void* ln_b, double ln_eps,
+                const void* W, const void* bias, void* logits, int64_t nb, int64_t C, int64_t V, int dtype,
+                cudaStream_t s);
+
 }  // namespace esa

@@ -68,6 +68,9 @@ SIGNATURES = {
                                   _vp]),
     "esa_lightning_step": (_int, [_vp, _i64, _int, _vp, _vp, _int, _vp, _int, _i64, _i64, _f64,
                                   _f64, _f64, _vp]),
+    "esa_decode_block_scratch_bytes": (_sz, [_i64, _i64, _int]),
+    "esa_decode_block": (_int, [_vp] * 18 + [_i64, _i64, _int, _f64, _f64, _f64, _f64, _vp, _sz, _vp]),
+    "esa_decode_head": (_int, [_vp, _vp, _vp, _vp, _f64, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "esa_layer_workspace_bytes": (_sz, [_i64, _i64, _i64, _int, _int, _int]),
     "esa_layer_fwd": (_int, [_vp, _i64, _int, _vp, _int, _vp, _int, _vp, _i64, _i64, _i64, _f64, _f64, _f64,
                              _vp, _vp, _vp, _sz, _vp]),

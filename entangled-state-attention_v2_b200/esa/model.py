@@ -171,7 +171,13 @@ class _ESABlock(nn.Module):
 
     def fused_lightning_step(self, x: torch.Tensor, pending: torch.Tensor | None, state: torch.Tensor):
         """lightning_step(x + pending) as (x', pending', new state), the residual
-        adds fused into the norms (see fused_forward)."""
+        adds fused into the norms (see fused_forward).  A few rows of a 16-bit
+        model run the whole block in four fused launches (ops.decode_block)."""
+        if ops.decode_block_supported(x, self):
+            from .generation import _unwrap_backend
+            bk = _unwrap_backend(self.esa)
+            return ops.decode_block(x, pending, state, self, bk.gate_min, bk.gate_max, bk.eps, bk.qgv,
+                                    bk.out_proj)
         if pending is None:
             h = self.ln1(x)
         else:
@@ -396,6 +402,8 @@ class ESAModel(nn.Module):
         for index, block in enumerate(self.blocks):
             x, pending, s = block.fused_lightning_step(x, pending, states[index])
             new_states.append(s)
+        if ops.decode_head_supported(x, self.ln_f, self.lm_head):
+            return ops.decode_head(x, pending, self.ln_f, self.lm_head), torch.stack(new_states, dim=0).contiguous()
         h = self.ln_f(x) if pending is None else self.ln_f.add_forward(x, pending)[1]
         return self.lm_head(h), torch.stack(new_states, dim=0).contiguous()
 

@@ -349,6 +349,77 @@ def _(qgv, state, gate_min, gate_max, eps, z_dtype):
     return (state.new_empty(nb, c3 // 3), qgv.new_empty(nb, c3 // 3, dtype=z_dtype))
 
 
+DECODE_MAX_ROWS = 4
+
+
+def _ptr_or_none(t):
+    return None if t is None else t.data_ptr()
+
+
+def decode_block_supported(x: Tensor, block) -> bool:
+    """The fused decode kernels apply: 1..4 rows of an fp16 or bf16 model
+    (every weight, the stream and the state in that dtype), C a multiple of
+    256, no gradient and no active dropout."""
+    if not x.is_cuda or x.dtype not in (torch.float16, torch.bfloat16) or torch.is_grad_enabled():
+        return False
+    if x.ndim != 2 or not (1 <= x.shape[0] <= DECODE_MAX_ROWS) or x.shape[1] % 256 != 0:
+        return False
+    if block.training:
+        return False
+    return all(p.dtype == x.dtype and p.is_contiguous() for p in block.parameters())
+
+
+def decode_head_supported(x: Tensor, ln_f, head) -> bool:
+    """esa_decode_head applies to these rows (see decode_block_supported)."""
+    if not x.is_cuda or x.dtype not in (torch.float16, torch.bfloat16) or torch.is_grad_enabled():
+        return False
+    if x.ndim != 2 or not (1 <= x.shape[0] <= DECODE_MAX_ROWS) or x.shape[1] % 256 != 0:
+        return False
+    return all(p.dtype == x.dtype and p.is_contiguous() for p in (*ln_f.parameters(), *head.parameters()))
+
+
+def decode_block(x: Tensor, pending: Optional[Tensor], state: Tensor, block, gate_min: float,
+                 gate_max: float, eps: float, qgv_lin, out_lin) -> tuple[Tensor, Tensor, Tensor]:
+    """One ESAModel block's decode step in four launches (C ABI
+    esa_decode_block): returns (x', pending', new state)."""
+    nb, C = x.shape
+    x = x.contiguous()
+    pending = None if pending is None else pending.contiguous()
+    st = state.reshape(nb, C).contiguous()
+    x_out = torch.empty_like(x)
+    p_out = torch.empty_like(x)
+    new_state = torch.empty_like(st)
+    code = dtype_code(x.dtype)
+    L = _lib.lib()
+    nbytes = L.esa_decode_block_scratch_bytes(nb, C, code)
+    scratch = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=x.device)
+    ln1, ln2, fc, proj = block.ln1, block.ln2, block.mlp.fc, block.mlp.proj
+    rc = L.esa_decode_block(x.data_ptr(), _ptr_or_none(pending), x_out.data_ptr(), p_out.data_ptr(),
+                            st.data_ptr(), new_state.data_ptr(), ln1.weight.data_ptr(), _ptr_or_none(ln1.bias),
+                            qgv_lin.weight.data_ptr(), _ptr_or_none(qgv_lin.bias), out_lin.weight.data_ptr(),
+                            _ptr_or_none(out_lin.bias), ln2.weight.data_ptr(), _ptr_or_none(ln2.bias),
+                            fc.weight.data_ptr(), _ptr_or_none(fc.bias), proj.weight.data_ptr(),
+                            _ptr_or_none(proj.bias), nb, C, code, float(gate_min), float(gate_max), float(eps),
+                            1e-5, scratch.data_ptr(), scratch.numel(), _stream(x))
+    _lib.check(rc, "esa_decode_block")
+    return x_out, p_out, new_state.reshape(state.shape)
+
+
+def decode_head(x: Tensor, pending: Optional[Tensor], ln_f, head) -> Tensor:
+    """logits = head(ln_f(x + pending)) for the rows of a decode step (C ABI
+    esa_decode_head)."""
+    nb, C = x.shape
+    V = head.weight.shape[0]
+    logits = torch.empty(nb, V, dtype=x.dtype, device=x.device)
+    rc = _lib.lib().esa_decode_head(x.contiguous().data_ptr(),
+                                    _ptr_or_none(None if pending is None else pending.contiguous()),
+                                    ln_f.weight.data_ptr(), _ptr_or_none(ln_f.bias), 1e-5,
+                                    head.weight.data_ptr(), _ptr_or_none(head.bias), logits.data_ptr(), nb, C, V,
+                                    dtype_code(x.dtype), _stream(x))
+    _lib.check(rc, "esa_decode_head")
+    return logits
+
+
 def check_device_status(device=None) -> None:
     """Raise if a kernel on `device` reported a bounded wait that ran out."""
     if device is None:

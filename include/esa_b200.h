@@ -339,6 +339,42 @@ int esa_layer_bwd(const void *dy, int dy_dtype, const void *qgv, int64_t qgv_row
                   double gate_max, double eps, const void *e0, void *de0, void *workspace,
                   size_t workspace_bytes, void *stream);
 
+/* Scratch (bytes) of esa_decode_block for nb rows of C channels: 18 nb C
+ * (the block's intermediate activations).  0 for invalid arguments.  No
+ * counterpart in the reference (it has no native code). */
+size_t esa_decode_block_scratch_bytes(int64_t nb, int64_t C, int dtype);
+
+/* One ESAModel block's decode step for nb = 1..4 rows of 16-bit data (dtype
+ * fp16 or bf16 for every tensor; C a multiple of 256), in four launches:
+ *   s1 = x + pending (pending NULL: s1 = x),  h1 = LN1(s1),
+ *   qgv = qgv_w h1 + qgv_b,  the Lightning step state -> new_state and its
+ *   readout z (as esa_lightning_step),  y = out_w z + out_b,
+ *   x_out = s1 + y,  h2 = LN2(x_out),  a = GELU(fc_w h2 + fc_b),
+ *   pending_out = proj_w a + proj_b.
+ * Activations are [nb, C] (qgv [nb, 3C], a [nb, 4C] in the scratch),
+ * weights are PyTorch Linear layouts ([out, in], row-major), every bias and
+ * LayerNorm bias may be NULL.  Each result is rounded to the 16-bit dtype
+ * where the PyTorch path rounds it (fp32 accumulation).  new_state must not
+ * alias state; x_out may alias x and pending_out pending.  The caller adds
+ * the last block's pending_out (esa_decode_head does).  Replaces one block of
+ * ESAModel.lightning_step (esa/model.py:717-757: ln_1, ESA.decode_step =
+ * esa/generation.py:410-469, residual add, ln_2, MLP, residual add). */
+int esa_decode_block(const void *x, const void *pending, void *x_out, void *pending_out,
+                     const void *state, void *new_state, const void *ln1_w, const void *ln1_b,
+                     const void *qgv_w, const void *qgv_b, const void *out_w, const void *out_b,
+                     const void *ln2_w, const void *ln2_b, const void *fc_w, const void *fc_b,
+                     const void *proj_w, const void *proj_b, int64_t nb, int64_t C, int dtype,
+                     double gate_min, double gate_max, double eps, double ln_eps, void *scratch,
+                     size_t scratch_bytes, void *stream);
+
+/* The decode step's head: logits [nb, V] = W LN_f(x + pending) + bias
+ * (pending and bias nullable; W [V, C], the tied embedding matrix), same
+ * dtypes and limits as esa_decode_block.  Replaces ESAModel.lightning_step's
+ * ln_f and lm_head (esa/model.py:717-757). */
+int esa_decode_head(const void *x, const void *pending, const void *ln_w, const void *ln_b, double ln_eps,
+                    const void *W, const void *bias, void *logits, int64_t nb, int64_t C, int64_t V,
+                    int dtype, void *stream);
+
 /* One ESA-Lightning decode step for nb rows, fused: gate nonlinearity, state
  * update and the RMS readout over all C = H*D channels.
  *   qgv: [nb, 3C] rows `qgv_row_stride` elements apart (q | gate | value)

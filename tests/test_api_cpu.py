@@ -28,7 +28,31 @@ def test_header_declares_the_abi():
         "esa_wait_selftest", "esa_readout_fwd", "esa_readout_bwd", "esa_layer_norm_fwd",
         "esa_layer_norm_workspace_bytes", "esa_layer_norm_bwd", "esa_add_layer_norm_fwd",
         "esa_add_layer_norm_bwd", "esa_cross_entropy_fwd", "esa_cross_entropy_bwd",
-        "esa_layer_workspace_bytes", "esa_layer_fwd", "esa_layer_bwd"}
+        "esa_layer_workspace_bytes", "esa_layer_fwd", "esa_layer_bwd",
+        "esa_decode_block_scratch_bytes", "esa_decode_block", "esa_decode_head"}
+
+
+def test_decode_entry_points_reject_bad_arguments_without_device_work():
+    """The fused decode kernels take 1..4 rows of fp16/bf16 data with C a
+    multiple of 256; everything else is refused by the host checks."""
+    from esa import _lib
+    L = _lib.lib()
+    assert L.esa_decode_block_scratch_bytes(1, 1024, _lib.DTYPE_F16) == 18 * 1024
+    assert L.esa_decode_block_scratch_bytes(4, 1024, _lib.DTYPE_BF16) == 18 * 4 * 1024
+    for nb, C, dt in ((0, 1024, _lib.DTYPE_F16), (5, 1024, _lib.DTYPE_F16), (1, 1000, _lib.DTYPE_F16),
+                      (1, 1024, _lib.DTYPE_F32)):
+        assert L.esa_decode_block_scratch_bytes(nb, C, dt) == 0
+        rc = L.esa_decode_block(*([None] * 18), nb, C, dt, 0.8, 0.995, 1e-5, 1e-5, None, 0, None)
+        assert rc != 0
+        assert "decode" in _lib.last_error()
+        rc = L.esa_decode_head(None, None, None, None, 1e-5, None, None, None, nb, C, 32000, dt, None)
+        assert rc != 0
+    # a valid shape without a scratch buffer is refused before any launch
+    rc = L.esa_decode_block(*([None] * 18), 1, 1024, _lib.DTYPE_F16, 0.8, 0.995, 1e-5, 1e-5, None, 0, None)
+    assert rc != 0 and "scratch" in _lib.last_error()
+    # a successful call (zero rows) clears this thread's error message again
+    assert L.esa_lightning_step(None, 3, 0, None, None, 0, None, 0, 0, 1, 0.8, 0.995, 1e-5, None) == 0
+    assert _lib.last_error() == ""
 
 
 def test_library_loads_and_exports_every_declared_symbol():
