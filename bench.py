@@ -199,6 +199,7 @@ def _timed(ctx, fn, steps: int, stream=None) -> tuple[float, float, dict]:
     stream = stream or torch.cuda.current_stream(ctx.dev)
     clocks = ClockSampler(ctx.local).start()
     time.sleep(0.3)
+    fn()  # one more untimed step after the sampler's start-up pause (the GPU idled meanwhile)
     ctx.barrier()
     torch.cuda.synchronize(ctx.dev)
     ev0 = torch.cuda.Event(enable_timing=True)
