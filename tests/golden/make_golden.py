@@ -2,14 +2,14 @@
 
 The reference (maxzameer/Entangled-State-Attention_v2, v2.1.1) is pure Python on
 PyTorch, so it can be imported on a CPU-only machine.  This script imports it from
-``/root/reference`` (override with ``ESA_REFERENCE_PATH``), runs the reference
-functions on seeded inputs and stores inputs plus outputs as compressed ``.npz``
-files.  The files are committed; the test suite and the GPU box never read the
-reference itself.
+the checkout named by ``ESA_REFERENCE_PATH`` (the directory holding ``esa/``),
+runs the reference functions on seeded inputs and stores inputs plus outputs as
+compressed ``.npz`` files.  The files are committed; the test suite and the GPU
+box never read the reference itself.
 
 Run from the repository root::
 
-    python tests/golden/make_golden.py
+    ESA_REFERENCE_PATH=<reference checkout> python tests/golden/make_golden.py
 
 Fixtures produced (all small enough for git):
 
