@@ -212,8 +212,11 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_gemv_kernel(const DecAr
             float* row = xs + b * K;
             float ss = 0.0f;
             for (int64_t c = threadIdx.x; c < K; c += kDecThreads) {
-                const float A = a.gmin + a.gspan * sigmoid_(Elem<T>::to_acc(q[K + c]));
-                const float B = (1.0f - A) * tanh_(Elem<T>::to_acc(q[2 * K + c]));
+                // the hardware approximations of the 16-bit gated scans: their
+                // errors sit below the 16-bit rounding of A, B and the state
+                const float A = fmaf(0.5f * a.gspan, tanh_fast(0.5f * Elem<T>::to_acc(q[K + c])),
+                                     a.gmin + 0.5f * a.gspan);
+                const float B = (1.0f - A) * tanh_fast(Elem<T>::to_acc(q[2 * K + c]));
                 // A and B cast to the state dtype before the update, as the reference does
                 const float sp = rnd<T>(rnd<T>(A) * Elem<T>::to_acc(st[b * K + c]) + rnd<T>(B));
                 if (c >= c0 && c < c1) ns[b * K + c] = Elem<T>::from_acc(sp);
@@ -222,7 +225,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_gemv_kernel(const DecAr
             }
             const float rr = 1.0f / sqrtf(cta_sum(ss, red) / (float)K + a.eps);
             for (int64_t c = threadIdx.x; c < K; c += kDecThreads)
-                row[c] = rnd<T>(sigmoid_(Elem<T>::to_acc(q[c])) * row[c] * rr);
+                row[c] = rnd<T>(sigmoid_fast(Elem<T>::to_acc(q[c])) * row[c] * rr);
         }
     }
     __syncthreads();
