@@ -256,6 +256,8 @@ class ESAModel(nn.Module):
         self._training_compile_failed = False
         self._compile_warnings_emitted: set[str] = set()
         self._decode_graphs: dict[tuple[Any, ...], Any] = {}
+        self._prefill_graphs: dict[tuple[Any, ...], Any] = {}
+        self._prefill_graph_failures: set[tuple[Any, ...]] = set()
         self.to(target)
 
     def _init_weights(self, module: nn.Module) -> None:
@@ -424,6 +426,29 @@ class ESAModel(nn.Module):
             self._warn_compile_fallback("runtime", exc)
         return self
 
+    def _prefill_for_generate(self, input_ids: torch.Tensor, engine: str, compile_mode: str, use_graph: bool):
+        """generate()'s prefill: with graph decoding on a GPU and an eager
+        (not compiled) engine, a captured CUDA graph per prompt shape
+        (decode_graph.PrefillGraph); otherwise prefill()."""
+        spec = parse_engine_spec(engine)
+        if use_graph and self.device.type == "cuda" and not spec.compiled and input_ids.ndim == 2:
+            ids = input_ids[:, -self.config.block:] if input_ids.size(1) > self.config.block else input_ids
+            key = (tuple(ids.shape), spec.backend, spec.compass, self.wte.weight.dtype)
+            if key not in self._prefill_graph_failures:
+                from .decode_graph import PrefillGraph
+                g = self._prefill_graphs.get(key)
+                if g is None:
+                    g = PrefillGraph(self, tuple(ids.shape), spec.backend, spec.compass)
+                    self._prefill_graphs[key] = g
+                try:
+                    logits, states, T = g.run(ids)
+                    return logits.clone(), states, T
+                except Exception as exc:  # capture refused (e.g. a host sync on the path)
+                    self._prefill_graphs.pop(key, None)
+                    self._prefill_graph_failures.add(key)
+                    self._warn_compile_fallback("prefill graph", exc)
+        return self.prefill(input_ids, engine=engine, compile_mode=compile_mode, fullgraph=False, dynamic=True)
+
     def _decode_graph(self, batch: int, state_dtype: torch.dtype, temperature, top_k, top_p):
         from .decode_graph import DecodeGraph
         key = (batch, state_dtype, float(temperature), top_k, top_p)
@@ -495,9 +520,8 @@ class ESAModel(nn.Module):
             prompt_tokens = int(input_ids.size(1))
             sync()
             total_start = time.perf_counter()
-            logits, states, prefill_len = self.prefill(input_ids, engine=prefill,
-                                                       compile_mode=compile_mode, fullgraph=False,
-                                                       dynamic=True)
+            logits, states, prefill_len = self._prefill_for_generate(input_ids, prefill, compile_mode,
+                                                                     use_graph)
             if states.is_cuda:
                 states = states.clone()
             sync()

@@ -158,3 +158,21 @@ def test_greedy_decode_graph_equals_eager_with_fused_kernels():
     b = model.generate(input_ids=ids, seek=24, prefill="thunder_16", temperature=0.0, compile=False,
                        decode_graph=False)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_graph_prefill_equals_eager_prefill(dtype):
+    """generate() with graph decoding replays a captured prefill per prompt
+    shape: its logits and states equal the eager prefill's bits, on a first
+    (capturing) and a second (replaying) prompt of the same shape."""
+    model = _small_model(dtype)
+    g = torch.Generator().manual_seed(13)
+    for _ in range(2):
+        ids = torch.randint(0, 2048, (2, 37), generator=g).cuda()
+        with torch.inference_mode():
+            logits, states, T = model._prefill_for_generate(ids, "thunder_16", "default", True)
+            ref_logits, ref_states, ref_T = model._prefill_eager(ids, backend="thunder", compass=16)
+        assert T == ref_T == 37
+        assert torch.equal(logits, ref_logits)
+        assert torch.equal(states, ref_states)
+    assert len(model._prefill_graphs) == 1 and not model._prefill_graph_failures
