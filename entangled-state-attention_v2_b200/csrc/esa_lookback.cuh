@@ -68,20 +68,45 @@ __device__ __forceinline__ void lookback(const Workspace& ws, unsigned* status, 
             const unsigned pm = ip & mm;
             const int p = pm ? (__ffs(pm) - 1) : -1;
             const int nagg = (p >= 0) ? p : m;
-            for (int q = 0; q < nagg; ++q) {
-                const int64_t jo = (k - (consumed + q + 1) * nct) * wch + lane * VEC;
-#pragma unroll
-                for (int v = 0; v < VEC; ++v) {
-                    const acc aj = __ldcg(agg_a + jo + v);
-                    const acc bj = __ldcg(agg_b + jo + v);
-                    cb[v] = ca[v] * bj + cb[v];
-                    ca[v] = ca[v] * aj;
-                }
-            }
+            // the prefix's load and the aggregates' loads go out together,
+            // the aggregates a few predecessors at a time (independent loads
+            // in flight instead of one L2 round trip per predecessor); the
+            // composition order is unchanged
+            acc pv[VEC];
             if (p >= 0) {
                 const int64_t jo = (k - (consumed + p + 1) * nct) * wch + lane * VEC;
 #pragma unroll
-                for (int v = 0; v < VEC; ++v) x[v] = ca[v] * __ldcg(pref + jo + v) + cb[v];
+                for (int v = 0; v < VEC; ++v) pv[v] = __ldcg(pref + jo + v);
+            }
+            // (two at a time for 32-byte lane vectors, which keep more in registers)
+            constexpr int PB = VEC * (int)sizeof(acc) >= 32 ? 2 : 4;
+            for (int q0 = 0; q0 < nagg; q0 += PB) {
+                acc ra[PB][VEC], rb[PB][VEC];
+#pragma unroll
+                for (int u = 0; u < PB; ++u) {
+                    if (q0 + u < nagg) {
+                        const int64_t jo = (k - (consumed + q0 + u + 1) * nct) * wch + lane * VEC;
+#pragma unroll
+                        for (int v = 0; v < VEC; ++v) {
+                            ra[u][v] = __ldcg(agg_a + jo + v);
+                            rb[u][v] = __ldcg(agg_b + jo + v);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < PB; ++u) {
+                    if (q0 + u < nagg) {
+#pragma unroll
+                        for (int v = 0; v < VEC; ++v) {
+                            cb[v] = ca[v] * rb[u][v] + cb[v];
+                            ca[v] = ca[v] * ra[u][v];
+                        }
+                    }
+                }
+            }
+            if (p >= 0) {
+#pragma unroll
+                for (int v = 0; v < VEC; ++v) x[v] = ca[v] * pv[v] + cb[v];
                 break;
             }
             consumed += m;
