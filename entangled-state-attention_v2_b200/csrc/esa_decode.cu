@@ -360,6 +360,9 @@ int check_shape(int64_t nb, int64_t C, int dtype) {
     return ESA_OK;
 }
 
+// The GEMVs read weight rows with 16-byte loads.
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 }  // namespace
 
 size_t decode_block_scratch_bytes(int64_t nb, int64_t C, int dtype) {
@@ -377,6 +380,8 @@ int decode_block(const DecodeBlock& p, cudaStream_t s) {
         !p.ln2_w || !p.fc_w || !p.proj_w)
         return set_error(ESA_ERR_INVALID_ARGUMENT, "null tensor pointer");
     if (p.state == p.new_state) return set_error(ESA_ERR_INVALID_ARGUMENT, "new_state must not alias state");
+    if (!aligned16(p.qgv_w) || !aligned16(p.out_w) || !aligned16(p.fc_w) || !aligned16(p.proj_w))
+        return set_error(ESA_ERR_INVALID_ARGUMENT, "decode weight matrices must be 16-byte aligned");
     const int64_t nb = p.nb, C = p.C;
     char* sc = static_cast<char*>(p.scratch);
     void* s1 = sc;
@@ -446,6 +451,7 @@ int decode_head(const void* x, const void* pending, const void* ln_w, const void
     if (int rc = check_shape(nb, C, dtype)) return rc;
     if (V <= 0) return set_error(ESA_ERR_INVALID_ARGUMENT, "vocabulary size must be positive");
     if (!x || !ln_w || !W || !logits) return set_error(ESA_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(W)) return set_error(ESA_ERR_INVALID_ARGUMENT, "decode weight matrices must be 16-byte aligned");
     DecArgs a{};
     a.nb = (int)nb;
     a.x = x;

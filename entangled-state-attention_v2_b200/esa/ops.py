@@ -366,7 +366,7 @@ def decode_block_supported(x: Tensor, block) -> bool:
         return False
     if block.training:
         return False
-    return all(p.dtype == x.dtype and p.is_contiguous() for p in block.parameters())
+    return all(p.dtype == x.dtype and p.is_contiguous() and p.data_ptr() % 16 == 0 for p in block.parameters())
 
 
 def decode_head_supported(x: Tensor, ln_f, head) -> bool:
@@ -375,7 +375,8 @@ def decode_head_supported(x: Tensor, ln_f, head) -> bool:
         return False
     if x.ndim != 2 or not (1 <= x.shape[0] <= DECODE_MAX_ROWS) or x.shape[1] % 256 != 0:
         return False
-    return all(p.dtype == x.dtype and p.is_contiguous() for p in (*ln_f.parameters(), *head.parameters()))
+    return all(p.dtype == x.dtype and p.is_contiguous() and p.data_ptr() % 16 == 0
+               for p in (*ln_f.parameters(), *head.parameters()))
 
 
 def decode_block(x: Tensor, pending: Optional[Tensor], state: Tensor, block, gate_min: float,

@@ -353,7 +353,8 @@ size_t esa_decode_block_scratch_bytes(int64_t nb, int64_t C, int dtype);
  *   pending_out = proj_w a + proj_b.
  * Activations are [nb, C] (qgv [nb, 3C], a [nb, 4C] in the scratch),
  * weights are PyTorch Linear layouts ([out, in], row-major), every bias and
- * LayerNorm bias may be NULL.  Each result is rounded to the 16-bit dtype
+ * LayerNorm bias may be NULL; the four weight matrices must start on a
+ * 16-byte boundary.  Each result is rounded to the 16-bit dtype
  * where the PyTorch path rounds it (fp32 accumulation).  new_state must not
  * alias state; x_out may alias x and pending_out pending.  The caller adds
  * the last block's pending_out (esa_decode_head does).  Replaces one block of

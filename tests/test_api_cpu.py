@@ -47,6 +47,9 @@ def test_decode_entry_points_reject_bad_arguments_without_device_work():
         assert "decode" in _lib.last_error()
         rc = L.esa_decode_head(None, None, None, None, 1e-5, None, None, None, nb, C, 32000, dt, None)
         assert rc != 0
+    # misaligned weight rows (the GEMVs read 16-byte vectors) are refused
+    rc = L.esa_decode_head(16, None, 16, None, 1e-5, 18, None, 16, 1, 1024, 32000, _lib.DTYPE_F16, None)
+    assert rc != 0 and "aligned" in _lib.last_error()
     # a valid shape without a scratch buffer is refused before any launch
     rc = L.esa_decode_block(*([None] * 18), 1, 1024, _lib.DTYPE_F16, 0.8, 0.995, 1e-5, 1e-5, None, 0, None)
     assert rc != 0 and "scratch" in _lib.last_error()
