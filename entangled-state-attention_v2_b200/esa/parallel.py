@@ -38,7 +38,7 @@ def compose_carries(summaries: list[torch.Tensor], rank: int,
     carry = torch.zeros_like(e_end0) if e0 is None else e0.to(e_end0.dtype).reshape(e_end0.shape)
     for r in range(rank):
         e_end, prod = summaries[r][0], summaries[r][1]
-        carry = prod * carry + e_end
+        carry = torch.addcmul(e_end, prod, carry)
     return carry
 
 
@@ -70,13 +70,16 @@ def sequence_parallel_scan(A: torch.Tensor, B: torch.Tensor, *, group=None, comp
     L = _lib.lib()
     stream = torch.cuda.current_stream(A.device).cuda_stream
     ws = ops._workspace(nb, T, hd, A.dtype, int(compass), A.device)
-    e_end = torch.zeros(nb, hd, dtype=acc, device=A.device)
-    prod = torch.ones(nb, hd, dtype=acc, device=A.device)
+    # [E_end, prod] written in place by the summary kernel (every channel of
+    # both), so the gather reads it without a stack copy
+    mine = torch.empty(2, nb, hd, dtype=acc, device=A.device)
     if T > 0 and hd > 0 and nb > 0:
         _lib.check(L.esa_scan_summary(A.data_ptr(), B.data_ptr(), nb, T, hd, code, None,
-                                      e_end.data_ptr(), prod.data_ptr(), ws.data_ptr(), ws.numel(),
+                                      mine[0].data_ptr(), mine[1].data_ptr(), ws.data_ptr(), ws.numel(),
                                       stream), "esa_scan_summary")
-    mine = torch.stack([e_end, prod])
+    else:
+        mine[0].zero_()
+        mine[1].fill_(1)
     if dist.get_backend(group) == "gloo":
         # gloo gathers host tensors: the 2*B*H*D summaries cross to the host
         # and back (ranks that share one GPU, or no NVLink)
@@ -85,8 +88,10 @@ def sequence_parallel_scan(A: torch.Tensor, B: torch.Tensor, *, group=None, comp
         dist.all_gather(gathered, host, group=group)
         gathered = [t.to(A.device) for t in gathered]
     else:
-        gathered = [torch.empty_like(mine) for _ in range(world)]
-        dist.all_gather(gathered, mine, group=group)
+        # one flat buffer: a single all_gather_into_tensor instead of a list
+        flat = torch.empty(world * 2, nb, hd, dtype=acc, device=A.device)
+        dist.all_gather_into_tensor(flat, mine, group=group)
+        gathered = list(flat.view(world, 2, nb, hd).unbind(0))
     carry = compose_carries(gathered, rank, e0).contiguous()
     E = torch.empty_like(A)
     if T > 0 and hd > 0 and nb > 0:
