@@ -664,12 +664,20 @@ def sp_leg(ctx) -> dict:
     B = (torch.randn(nb, Tr, H, D, device=dev, generator=g) * 0.5).to(torch.bfloat16)
     out_box = {}
 
-    def step():
+    def step(form="single_pass"):
         if ws > 1:
-            out_box["E"] = sequence_parallel_scan(A, B)
+            out_box["E"] = sequence_parallel_scan(A, B, form=form)
         else:
             out_box["E"] = ops.scan(A, B, None, 16)[0]
 
+    # the two-pass form first, for comparison (same inputs, same ranks)
+    two_pass_ms = None
+    if ws > 1:
+        for _ in range(3):
+            step("two_pass")
+        torch.cuda.synchronize(dev)
+        two_total, _, _ = _timed(ctx, lambda: step("two_pass"), steps)
+        two_pass_ms = two_total / steps
     for _ in range(3):
         step()
     torch.cuda.synchronize(dev)
@@ -688,9 +696,13 @@ def sp_leg(ctx) -> dict:
         "data": "synthetic (seeded per rank)",
         "config": {"workload": "long-sequence scan [4,262144,32,64] bf16, T split across ranks",
                    "form": "plain scan of the whole sequence" if ws == 1 else
-                   "slice summary + NCCL all_gather of [2,4,2048] fp32 + scan from the exact incoming "
-                   "state (5 bytes-per-element passes)",
+                   "single pass: slice scan from zero + product of A (stops where it is zero) + NCCL "
+                   "all_gather of [2,4,2048] fp32 + rescan of the slice head from the exact incoming state",
                    "parallelism": f"sp{ws}"},
+        "two_pass": None if two_pass_ms is None else {
+            "ms_per_step": two_pass_ms, "value": alg / (two_pass_ms * 1e-3) / 1e9,
+            "form": "slice summary + all_gather + scan from the exact incoming state (5 bytes-per-element "
+                    "passes)"},
         "roofline": {"bound": "hbm", "achieved": val / ws, "peak": peak, "unit": "GB/s",
                      "frac": val / ws / peak, "peak_kind": pk, "note": "per GPU, algorithmic 3N bytes"},
         "clocks": clk,

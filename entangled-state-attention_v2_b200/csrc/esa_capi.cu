@@ -219,6 +219,18 @@ ESA_EXPORT int esa_scan_summary(const void* A, const void* B, int64_t nb, int64_
                         static_cast<cudaStream_t>(stream));
 }
 
+ESA_EXPORT int esa_scan_prod(const void* A, void* prod, int64_t nb, int64_t T, int64_t hd, int dtype,
+                             void* stream) {
+    clear_error();
+    return scan_prod(A, prod, nb, T, hd, dtype, static_cast<cudaStream_t>(stream));
+}
+
+ESA_EXPORT int esa_scan_fixup(const void* A, const void* B, void* E, const void* carry, int64_t nb, int64_t T,
+                              int64_t hd, int dtype, void* stream) {
+    clear_error();
+    return scan_fixup(A, B, E, carry, nb, T, hd, dtype, static_cast<cudaStream_t>(stream));
+}
+
 ESA_EXPORT int esa_scan_rev(const void* A, const void* E, const void* dE, void* dA, void* dB, int64_t nb,
                  int64_t T, int64_t hd, int dtype, int compass, const void* e0, void* de0,
                  void* workspace, size_t workspace_bytes, void* stream) {

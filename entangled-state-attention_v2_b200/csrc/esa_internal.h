@@ -115,6 +115,9 @@ int gated_scan_bwd(const void* g, const void* v, int64_t rrs, int raw_dtype, con
                    cudaStream_t s);
 int scan_summary(const void* A, const void* B, int64_t nb, int64_t T, int64_t hd, int dtype,
                  const void* e0, void* e_last, void* prod, void* ws, size_t ws_bytes, cudaStream_t s);
+int scan_prod(const void* A, void* prod, int64_t nb, int64_t T, int64_t hd, int dtype, cudaStream_t s);
+int scan_fixup(const void* A, const void* B, void* E, const void* carry, int64_t nb, int64_t T, int64_t hd,
+               int dtype, cudaStream_t s);
 size_t scan_workspace_bytes(int64_t nb, int64_t T, int64_t hd, int wide_es, int compass);
 size_t scan_host_staging_bytes(int64_t nb, int64_t T, int64_t hd, int es, int compass);
 int scan_fwd_host(const void* A, const void* B, void* E, int64_t nb, int64_t T, int64_t hd, int dtype,

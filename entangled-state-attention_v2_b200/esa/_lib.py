@@ -59,6 +59,8 @@ SIGNATURES = {
     "esa_scan_fwd_host": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _sz, _vp]),
     "esa_scan_fwd_resume": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _sz, _vp]),
     "esa_scan_summary": (_int, [_vp, _vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "esa_scan_prod": (_int, [_vp, _vp, _i64, _i64, _i64, _int, _vp]),
+    "esa_scan_fixup": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _vp]),
     "esa_scan_rev": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp,
                             _sz, _vp]),
     "esa_gated_scan_fwd": (_int, [_vp, _vp, _i64, _int, _vp, _int, _i64, _i64, _i64, _f64, _f64,

@@ -245,6 +245,29 @@ int esa_scan_summary(const void *A, const void *B, int64_t nb, int64_t T, int64_
                      const void *e0, void *e_last, void *prod, void *workspace,
                      size_t workspace_bytes, void *stream);
 
+/* Product of A over the time axis: prod[b*hd + c] = A[b,0,c] * ... *
+ * A[b,T-1,c] in the acc type, [nb, hd].  Reads A from t = 0 and stops once
+ * the running product is exactly zero for every channel of a block (gates
+ * below one reach zero after a few thousand steps; A = 1 reads all of A).
+ * No workspace.  With the end state of esa_scan_fwd from a zero state
+ * (e_last), this is a time slice's summary for esa_scan_summary's
+ * composition rule.  Replaces nothing in the reference (it has no
+ * multi-device path); part of the single-pass sequence-parallel scan. */
+int esa_scan_prod(const void *A, void *prod, int64_t nb, int64_t T, int64_t hd, int dtype,
+                  void *stream);
+
+/* Head of a time slice that esa_scan_fwd scanned from a zero state, rescanned
+ * once its true incoming state `carry` (acc type, [nb, hd]) is known:
+ *   E[b,t,c] = A[b,t,c] * x_{t-1} + B[b,t,c],  x_{-1} = carry[b*hd + c]
+ * (fp32 / fp64 state, each output rounded once to `dtype`), for t from 0
+ * until the product A[b,0,c] * ... * A[b,t,c] is exactly zero for every
+ * channel of a block; from there on the outputs of the scan from zero equal
+ * those from `carry` (to the rounding of the state) and are left as they
+ * are.  Replaces nothing in the reference (it has no multi-device path);
+ * part of the single-pass sequence-parallel scan (esa/parallel.py). */
+int esa_scan_fixup(const void *A, const void *B, void *E, const void *carry, int64_t nb, int64_t T,
+                   int64_t hd, int dtype, void *stream);
+
 /* esa_scan_fwd of a slice whose summary esa_scan_summary has just computed,
  * with the same A, B, shape, dtype and workspace (and no other call using the
  * workspace in between).  Few-channel, long slices are scanned in time pieces

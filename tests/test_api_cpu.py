@@ -23,7 +23,7 @@ def test_header_declares_the_abi():
     assert set(syms) == {
         "esa_abi_version", "esa_last_error", "esa_scan_last_path", "esa_device_status", "esa_scan_workspace_bytes",
         "esa_scan_fwd", "esa_scan_rev", "esa_gated_scan_fwd", "esa_gated_scan_bwd",
-        "esa_lightning_step", "esa_scan_fwd_noalloc", "esa_scan_summary",
+        "esa_lightning_step", "esa_scan_fwd_noalloc", "esa_scan_summary", "esa_scan_prod", "esa_scan_fixup",
         "esa_scan_host_staging_bytes", "esa_scan_fwd_host", "esa_scan_fwd_resume",
         "esa_wait_selftest", "esa_readout_fwd", "esa_readout_bwd", "esa_layer_norm_fwd",
         "esa_layer_norm_workspace_bytes", "esa_layer_norm_bwd", "esa_add_layer_norm_fwd",
@@ -55,6 +55,25 @@ def test_decode_entry_points_reject_bad_arguments_without_device_work():
     assert rc != 0 and "scratch" in _lib.last_error()
     # a successful call (zero rows) clears this thread's error message again
     assert L.esa_lightning_step(None, 3, 0, None, None, 0, None, 0, 0, 1, 0.8, 0.995, 1e-5, None) == 0
+    assert _lib.last_error() == ""
+
+
+def test_slice_prod_and_fixup_reject_bad_arguments_without_device_work():
+    """esa_scan_prod / esa_scan_fixup: empty problems are no-ops, bad sizes,
+    dtypes and null pointers are refused before any launch."""
+    from esa import _lib
+    L = _lib.lib()
+    assert L.esa_scan_prod(None, None, 0, 100, 64, _lib.DTYPE_F16, None) == 0
+    assert L.esa_scan_fixup(None, None, None, None, 4, 100, 0, _lib.DTYPE_BF16, None) == 0
+    assert L.esa_scan_prod(None, None, -1, 100, 64, _lib.DTYPE_F16, None) != 0
+    assert "negative" in _lib.last_error()
+    assert L.esa_scan_prod(None, None, 1, 100, 64, 9, None) != 0
+    assert "dtype" in _lib.last_error()
+    assert L.esa_scan_prod(None, None, 1, 100, 64, _lib.DTYPE_F32, None) != 0
+    assert "null" in _lib.last_error()
+    assert L.esa_scan_fixup(16, 16, 16, None, 1, 100, 64, _lib.DTYPE_F32, None) != 0
+    assert "null" in _lib.last_error()
+    assert L.esa_scan_prod(None, None, 0, 0, 0, _lib.DTYPE_F32, None) == 0
     assert _lib.last_error() == ""
 
 

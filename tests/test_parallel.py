@@ -135,13 +135,14 @@ def _nccl_worker(rank, world, port, q):
         cuts = [i * T // world for i in range(world + 1)]
         sl = slice(cuts[rank], cuts[rank + 1])
         E = sequence_parallel_scan(A[:, sl].cuda(), B[:, sl].cuda())
+        E2 = sequence_parallel_scan(A[:, sl].cuda(), B[:, sl].cuda(), form="two_pass")
         torch.cuda.synchronize()
-        q.put((rank, E.cpu().numpy()))
+        q.put((rank, (E.cpu().numpy(), E2.cpu().numpy())))
     finally:
         dist.destroy_process_group()
 
 
-def _one_gpu_worker(rank, world, port, backend, q):
+def _one_gpu_worker(rank, world, port, backend, form, q):
     """Rank of a sequence-parallel scan whose ranks all share GPU 0 (the
     kernels of different ranks never wait on one another: the only exchange is
     the all-gather between the summary and the scan)."""
@@ -162,7 +163,7 @@ def _one_gpu_worker(rank, world, port, backend, q):
         T = A.shape[1]
         cuts = [i * T // world for i in range(world + 1)]
         sl = slice(cuts[rank], cuts[rank + 1])
-        E = sequence_parallel_scan(A[:, sl].cuda(), B[:, sl].cuda(), e0=e0.cuda())
+        E = sequence_parallel_scan(A[:, sl].cuda(), B[:, sl].cuda(), e0=e0.cuda(), form=form)
         torch.cuda.synchronize()
         ops.check_device_status()
         q.put((rank, E.cpu().numpy()))
@@ -180,17 +181,19 @@ def _sp_inputs():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("form", ["single_pass", "two_pass"])
 @pytest.mark.parametrize("backend,world", [("nccl", 1), ("gloo", 2), ("gloo", 3)])
-def test_sequence_parallel_scan_on_one_gpu(backend, world):
-    """esa.parallel.sequence_parallel_scan end to end (summary kernel,
-    all-gather, carry composition, resumed scan) with every rank on GPU 0:
-    NCCL at world size 1, gloo at 2 and 3 (slices of 8192 steps or more, so
-    the few-channel slices take the split summary / resume path); the joined slices against the fp64 oracle of the
-    whole sequence from the same initial state."""
+def test_sequence_parallel_scan_on_one_gpu(backend, world, form):
+    """esa.parallel.sequence_parallel_scan end to end with every rank on
+    GPU 0: NCCL at world size 1, gloo at 2 and 3 (slices of 8192 steps or
+    more).  single_pass: scan from zero + product, all-gather, carry
+    composition, fix-up of the slice head; two_pass: split summary,
+    all-gather, resumed scan.  The joined slices against the fp64 oracle of
+    the whole sequence from the same initial state."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_one_gpu_worker, args=(r, world, port, backend, q)) for r in range(world)]
+    procs = [ctx.Process(target=_one_gpu_worker, args=(r, world, port, backend, form, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=300) for _ in range(world))
@@ -225,8 +228,9 @@ def test_sequence_parallel_scan_nccl():
     A = torch.sigmoid(torch.randn(nb, T, H, D, generator=g) + 3)
     B = torch.randn(nb, T, H, D, generator=g) * 0.5
     ref = oracle.scan_fwd(A.double(), B.double())
-    full = np.concatenate([got[r] for r in range(world)], axis=1)
-    assert np.linalg.norm(full - ref) / np.linalg.norm(ref) < 1e-5
+    for form in range(2):
+        full = np.concatenate([got[r][form] for r in range(world)], axis=1)
+        assert np.linalg.norm(full - ref) / np.linalg.norm(ref) < 1e-5
 
 
 @pytest.mark.gpu
@@ -264,3 +268,50 @@ def test_summary_then_resume_equals_full_scan(shape):
     torch.testing.assert_close(e_last, ref_last, rtol=1e-5, atol=1e-5)
     # the slice summary composes with e0 into the end state
     torch.testing.assert_close(prod * e0 + e_end, e_last, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,tol", [(torch.float16, 2e-3), (torch.bfloat16, 2e-3), (torch.float32, 1e-5),
+                                       (torch.float64, 1e-12)])
+@pytest.mark.parametrize("shape,gates", [((2, 5000, 4, 64), "sigmoid"), ((3, 700, 1, 77), "sigmoid"),
+                                         ((2, 3000, 2, 64), "ones"), ((1, 1, 2, 1024), "sigmoid")])
+def test_slice_prod_and_fixup_against_oracle(dtype, tol, shape, gates):
+    """esa_scan_prod (product of A over the slice, stopping where it is zero)
+    and esa_scan_fixup (the head of a slice scanned from zero, rescanned from
+    its incoming state) against the fp64 oracle: the result equals the scan
+    from e0 = carry.  Covers
+    16-bit channel pairs (even hd) and single channels (hd = 77), gates of one
+    everywhere (the product never reaches zero: both kernels walk the whole
+    slice) and a one-step slice (2048 channels: the 16-bit bar is a relative
+    Frobenius norm, meaningful over many elements)."""
+    from esa import _lib, ops
+    g = torch.Generator().manual_seed(21)
+    nb, T, H, D = shape
+    hd = H * D
+    if gates == "ones":
+        A = torch.ones(shape, dtype=torch.float64)
+    else:
+        A = torch.sigmoid(torch.randn(shape, generator=g, dtype=torch.float64) + 3)
+    A = A.to(dtype)
+    B = (torch.randn(shape, generator=g, dtype=torch.float64) * 0.5).to(dtype)
+    carry = torch.randn(nb, hd, generator=g, dtype=torch.float64)
+    acc = ops.acc_dtype(dtype)
+    Ad, Bd = A.cuda(), B.cuda()
+    E0, _ = ops.scan(Ad, Bd, None, 16)
+    L = _lib.lib()
+    s = torch.cuda.current_stream().cuda_stream
+    code = ops.dtype_code(dtype)
+    prod = torch.empty(nb, hd, dtype=acc, device="cuda")
+    _lib.check(L.esa_scan_prod(Ad.data_ptr(), prod.data_ptr(), nb, T, hd, code, s), "esa_scan_prod")
+    cd = carry.to(acc).cuda()
+    E = E0.clone()
+    _lib.check(L.esa_scan_fixup(Ad.data_ptr(), Bd.data_ptr(), E.data_ptr(), cd.data_ptr(), nb, T, hd, code, s),
+               "esa_scan_fixup")
+    torch.cuda.synchronize()
+    p_ref = np.prod(A.double().numpy(), axis=1).reshape(nb, hd)
+    np.testing.assert_allclose(prod.double().cpu().numpy(), p_ref, rtol=max(tol, 1e-3) if acc == torch.float32
+                               else 1e-10, atol=1e-30)
+    ref = oracle.scan_fwd(A.double(), B.double(), cd.double().cpu().reshape(nb, H, D))
+    got = E.double().cpu().numpy()
+    err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert err < tol, err
